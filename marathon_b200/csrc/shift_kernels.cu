@@ -1,0 +1,707 @@
+// shift_kernels.cu — sm_100a kernels of the position-shifted KV reuse path.
+//
+// Load (store -> paged cache, K re-rotated by each run's delta) and save
+// (paged cache -> store, bit copy) are one templated persistent kernel.  A
+// launch covers every (layer, run, token tile) of a batch: multi-layer,
+// multi-run and multi-session work is a single launch.
+//
+// Work decomposition.  A tile is up to `tile_tokens` consecutive tokens of
+// one run in one layer.  Tiles are numbered layer-major
+// (w = layer * tiles_per_layer + tile) and CTAs stride over them, so
+// neighbouring CTAs read neighbouring store rows and write neighbouring
+// paged blocks.  The run owning a tile is found by a uniform binary search
+// over the runs' tile_begin prefix.
+//
+// Per tile the CTA first resolves every token's paged offset (slot -> block,
+// offset; bounds-checked, bad tokens flagged and skipped) into shared memory
+// and stages the run's cos/sin table there.  Then G = head_size/(2*VEC)
+// threads cooperate on one (token, head) unit: each thread moves two 16-byte
+// K vectors and two 16-byte V vectors.  For K the two vectors are RoPE
+// partners (elements i and i + rotary/2), so the rotation
+//     out[i]        = k[i] * cos[i] - k[i+half] * sin[i]
+//     out[i + half] = k[i+half] * cos[i] + k[i] * sin[i]
+// needs no shuffle.  Every HBM access is a 128-bit coalesced load or store
+// and every byte is read once and written once.
+//
+// Arithmetic follows the reference's torch path term by term
+// (src/marathon/shift_kernels.py:153-156): two fp32 products, rounded
+// separately, then one fp32 add; no FMA contraction (__fmul_rn/__fadd_rn), so
+// the fp32 value before the final rounding is bit-identical to the CPU
+// computation and the stored element is its round-to-nearest-even.  E4M3:
+// code -> fp32 * k_scale, rotate, / k_scale, saturate to +-448, RNE.
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/marathon_shift.h"
+
+namespace mshift {
+
+constexpr int kThreads = 256;  // threads per CTA
+constexpr int kMaxTile = 256;  // tokens per tile, upper bound (smem sizing)
+constexpr int kMaxDevices = 64;
+
+struct alignas(16) Vec {
+  uint32_t w[4];
+};
+
+__device__ __forceinline__ Vec load_vec(const void* p) {
+  const uint4 r = __ldcs(reinterpret_cast<const uint4*>(p));
+  return Vec{{r.x, r.y, r.z, r.w}};
+}
+
+__device__ __forceinline__ void store_vec(void* p, const Vec& v) {
+  __stcs(reinterpret_cast<uint4*>(p), make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]));
+}
+
+// ---------------------------------------------------------------- element types
+struct Bf16 {
+  static constexpr int kBytes = 2, kVec = 8;
+  static constexpr bool kScaled = false;
+  __device__ static void unpack(const Vec& v, float* f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(v.w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(v.w[i] & 0xffff0000u);
+    }
+  }
+  __device__ static Vec pack(const float* f) {
+    Vec v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      v.w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return v;
+  }
+};
+
+struct F16 {
+  static constexpr int kBytes = 2, kVec = 8;
+  static constexpr bool kScaled = false;
+  __device__ static void unpack(const Vec& v, float* f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = *reinterpret_cast<const __half2*>(&v.w[i]);
+      const float2 p = __half22float2(h);
+      f[2 * i] = p.x;
+      f[2 * i + 1] = p.y;
+    }
+  }
+  __device__ static Vec pack(const float* f) {
+    Vec v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      v.w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return v;
+  }
+};
+
+struct F32 {
+  static constexpr int kBytes = 4, kVec = 4;
+  static constexpr bool kScaled = false;
+  __device__ static void unpack(const Vec& v, float* f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(v.w[i]);
+  }
+  __device__ static Vec pack(const float* f) {
+    Vec v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v.w[i] = __float_as_uint(f[i]);
+    return v;
+  }
+};
+
+struct E4m3 {
+  static constexpr int kBytes = 1, kVec = 16;
+  static constexpr bool kScaled = true;
+  __device__ static void unpack(const Vec& v, float* f) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const __nv_fp8x2_storage_t pair =
+            static_cast<__nv_fp8x2_storage_t>((v.w[i] >> (16 * j)) & 0xffffu);
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+        f[4 * i + 2 * j] = p.x;
+        f[4 * i + 2 * j + 1] = p.y;
+      }
+    }
+  }
+  __device__ static Vec pack(const float* f) {
+    Vec v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i], f[4 * i + 1]),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i + 2], f[4 * i + 3]),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      v.w[i] = (lo & 0xffffu) | ((hi & 0xffffu) << 16);
+    }
+    return v;
+  }
+};
+
+// Rotate one pair of partner vectors in place: `a` holds elements
+// [i0, i0+VEC) of the first rotary half, `b` the same elements of the second.
+template <class E>
+__device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, const float* sn,
+                                            float scale) {
+  constexpr int V = E::kVec;
+  float x[V], y[V], c[V], s[V];
+  E::unpack(a, x);
+  E::unpack(b, y);
+#pragma unroll
+  for (int e = 0; e < V; e += 4) {
+    const float4 c4 = *reinterpret_cast<const float4*>(cs + e);
+    const float4 s4 = *reinterpret_cast<const float4*>(sn + e);
+    c[e] = c4.x, c[e + 1] = c4.y, c[e + 2] = c4.z, c[e + 3] = c4.w;
+    s[e] = s4.x, s[e + 1] = s4.y, s[e + 2] = s4.z, s[e + 3] = s4.w;
+  }
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    float xe = x[e], ye = y[e];
+    if constexpr (E::kScaled) {
+      xe = __fmul_rn(xe, scale);
+      ye = __fmul_rn(ye, scale);
+    }
+    float ra = __fsub_rn(__fmul_rn(xe, c[e]), __fmul_rn(ye, s[e]));
+    float rb = __fadd_rn(__fmul_rn(ye, c[e]), __fmul_rn(xe, s[e]));
+    if constexpr (E::kScaled) {
+      ra = __fdiv_rn(ra, scale);
+      rb = __fdiv_rn(rb, scale);
+    }
+    x[e] = ra;
+    y[e] = rb;
+  }
+  a = E::pack(x);
+  b = E::pack(y);
+}
+
+// ------------------------------------------------------------------ arguments
+struct KArgs {
+  const mshift_run* runs;  // device; nullptr selects the single-run fields below
+  int32_t n_runs;
+  int32_t tile_tokens;
+  int32_t tiles_per_layer;
+  int32_t n_layers;
+  void* const* store_ptrs;   // [n_sessions * n_layers]
+  const int64_t* store_caps; // [n_sessions]
+  int32_t n_sessions;
+  int32_t block_size;
+  int64_t st_tok, st_head;   // store strides (elements)
+  void* const* k_ptrs;       // [n_layers]
+  void* const* v_ptrs;
+  int64_t blk_stride, off_stride, head_stride, num_slots;
+  int32_t heads;
+  int32_t n_tables;
+  const float* tables;       // [n_tables][2][half]
+  const float* k_scales;     // [n_layers] (E4M3 only)
+  uint32_t* err;
+  // single run, single layer (runs == nullptr)
+  mshift_run run0;
+  void* store0;
+  int64_t cap0;
+  void* k0;
+  void* v0;
+  const float* table0;
+};
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// One templated kernel for both directions.
+//   SAVE = false: store rows -> paged cache, K rotated (load)
+//   SAVE = true : paged cache -> store rows, bit copy (save)
+template <class E, int D, int ROT, bool SAVE>
+__global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
+  constexpr int ES = E::kBytes;
+  constexpr int VEC = E::kVec;
+  constexpr int NV = D / VEC;      // 16-byte vectors per K (or V) row
+  constexpr int HALF = ROT / 2;
+  constexpr int NP = HALF / VEC;   // rotating partner pairs per row
+  constexpr int G = NV / 2;        // threads per (token, head) unit
+  constexpr int UPP = kThreads / G;
+  static_assert(D % (2 * VEC) == 0, "head_size must hold an even number of 16-byte vectors");
+  static_assert(HALF % VEC == 0 && NP <= G, "rotary half must be whole vectors");
+  static_assert(kThreads % G == 0, "threads per unit must divide the CTA");
+
+  __shared__ int64_t s_off[kMaxTile];
+  __shared__ __align__(16) float s_cs[HALF > 0 ? HALF : 4];
+  __shared__ __align__(16) float s_sn[HALF > 0 ? HALF : 4];
+
+  const int g = threadIdx.x % G;
+  const int u_first = threadIdx.x / G;
+  // vector indices this thread moves in every K row: a partner pair when
+  // g < NP, else two pass-through vectors of the non-rotary tail.
+  const int ka = g < NP ? g : g + NP;
+  const int kb = g < NP ? g + NP : g + G;
+  const int total = a.tiles_per_layer * a.n_layers;
+
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int layer = w / a.tiles_per_layer;
+    const int tile = w - layer * a.tiles_per_layer;
+
+    mshift_run run;
+    char* store;
+    int64_t cap;
+    char* kbase;
+    char* vbase;
+    const float* tab = nullptr;
+    bool ok_desc = true;
+    uint32_t bits = 0;
+    if (a.runs != nullptr) {
+      int lo = 0, hi = a.n_runs - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
+      }
+      run = a.runs[lo];
+      const bool sess = run.session >= 0 && run.session < a.n_sessions;
+      store = sess ? static_cast<char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
+                   : nullptr;
+      cap = sess ? a.store_caps[run.session] : 0;
+      if (!sess || store == nullptr || !aligned16(store)) { ok_desc = false; bits |= MSHIFT_EBIT_SESSION; }
+      kbase = static_cast<char*>(a.k_ptrs[layer]);
+      vbase = static_cast<char*>(a.v_ptrs[layer]);
+      if (!SAVE) {
+        if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
+        else if (run.table != -1) { ok_desc = false; bits |= MSHIFT_EBIT_TABLE; }
+      }
+    } else {
+      run = a.run0;
+      store = static_cast<char*>(a.store0);
+      cap = a.cap0;
+      kbase = static_cast<char*>(a.k0);
+      vbase = static_cast<char*>(a.v0);
+      tab = SAVE ? nullptr : a.table0;
+    }
+    if (kbase == nullptr || vbase == nullptr || !aligned16(kbase) || !aligned16(vbase)) {
+      ok_desc = false;
+      bits |= MSHIFT_EBIT_SLOT;
+    }
+    const int t0 = (tile - run.tile_begin) * a.tile_tokens;
+    const int nt = min(a.tile_tokens, run.len - t0);
+    const bool tile_ok = ok_desc && nt > 0 && t0 >= 0;
+    const float kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
+
+    __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn
+    if (threadIdx.x == 0 && bits) atomicOr(a.err, bits);
+    if (tile_ok) {
+      for (int t = threadIdx.x; t < nt; t += kThreads) {
+        const int64_t spos = run.store_start + t0 + t;
+        int64_t slot;
+        bool slot_ok = true;
+        if (run.slots != nullptr) {
+          slot = run.slots[t0 + t];
+        } else {
+          const int64_t pos = run.paged_start + t0 + t;
+          const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
+          slot_ok = bi >= 0 && bi < run.block_table_len;
+          slot = slot_ok ? (int64_t)run.block_table[bi] * a.block_size + pos % a.block_size : -1;
+        }
+        slot_ok = slot_ok && slot >= 0 && slot < a.num_slots;
+        const bool store_ok = spos >= 0 && spos < cap;
+        s_off[t] = (slot_ok && store_ok)
+                       ? (slot / a.block_size) * a.blk_stride + (slot % a.block_size) * a.off_stride
+                       : -1;
+        if (!slot_ok || !store_ok)
+          atomicOr(a.err, (slot_ok ? 0u : MSHIFT_EBIT_SLOT) | (store_ok ? 0u : MSHIFT_EBIT_STORE));
+      }
+      if (!SAVE && HALF > 0 && tab != nullptr) {
+        for (int i = threadIdx.x; i < HALF; i += kThreads) {
+          s_cs[i] = tab[i];
+          s_sn[i] = tab[HALF + i];
+        }
+      }
+    }
+    __syncthreads();
+    if (!tile_ok) continue;
+
+    const bool rotate = !SAVE && HALF > 0 && tab != nullptr && g < NP;
+    const int nu = nt * a.heads;
+    const int64_t row0 = run.store_start + t0;
+    for (int u = u_first; u < nu; u += 2 * UPP) {
+      // two units per iteration: all eight loads are issued before any store
+      Vec k[2][2], v[2][2];
+      char* sp[2];
+      char* kp[2];
+      char* vp[2];
+      bool live[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int uu = u + q * UPP;
+        live[q] = false;
+        if (uu < nu) {
+          const int t = uu / a.heads;
+          const int h = uu - t * a.heads;
+          const int64_t off = s_off[t];
+          if (off >= 0) {
+            live[q] = true;
+            sp[q] = store + ((row0 + t) * a.st_tok + (int64_t)h * a.st_head) * ES;
+            kp[q] = kbase + (off + (int64_t)h * a.head_stride) * ES;
+            vp[q] = vbase + (off + (int64_t)h * a.head_stride) * ES;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (!live[q]) continue;
+        if (SAVE) {
+          k[q][0] = load_vec(kp[q] + ka * 16);
+          k[q][1] = load_vec(kp[q] + kb * 16);
+          v[q][0] = load_vec(vp[q] + g * 16);
+          v[q][1] = load_vec(vp[q] + (g + G) * 16);
+        } else {
+          k[q][0] = load_vec(sp[q] + ka * 16);
+          k[q][1] = load_vec(sp[q] + kb * 16);
+          v[q][0] = load_vec(sp[q] + D * ES + g * 16);
+          v[q][1] = load_vec(sp[q] + D * ES + (g + G) * 16);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (!live[q]) continue;
+        if (rotate) rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC, kscale);
+        if (SAVE) {
+          store_vec(sp[q] + ka * 16, k[q][0]);
+          store_vec(sp[q] + kb * 16, k[q][1]);
+          store_vec(sp[q] + D * ES + g * 16, v[q][0]);
+          store_vec(sp[q] + D * ES + (g + G) * 16, v[q][1]);
+        } else {
+          store_vec(kp[q] + ka * 16, k[q][0]);
+          store_vec(kp[q] + kb * 16, k[q][1]);
+          store_vec(vp[q] + g * 16, v[q][0]);
+          store_vec(vp[q] + (g + G) * 16, v[q][1]);
+        }
+      }
+    }
+  }
+}
+
+// cos/sin of fp32(delta) * inv_freq[i]: the angle is rounded to fp32 exactly
+// as the reference forms it (src/marathon/shift_kernels.py:73), then cos and
+// sin are evaluated in double precision and rounded once to fp32.
+__global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float* inv_freq,
+                                   int32_t half, float* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * half) return;
+  const int64_t d = i / half;
+  const int64_t j = i - d * half;
+  const float ang = __fmul_rn(static_cast<float>(deltas[d]), inv_freq[j]);
+  double s, c;
+  sincos(static_cast<double>(ang), &s, &c);
+  out[d * 2 * half + j] = __double2float_rn(c);
+  out[d * 2 * half + half + j] = __double2float_rn(s);
+}
+
+// ------------------------------------------------------------------ dispatch
+using KernelFn = void (*)(KArgs);
+
+struct Variant {
+  int32_t dtype, head_size, rotary;
+  KernelFn load;
+  KernelFn save;
+};
+
+#define MSHIFT_VARIANT(E, DT, D, R) \
+  {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>}
+
+const Variant kVariants[] = {
+    MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 128, 128),
+    MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 128, 64),
+    MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 64, 64),
+    MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 256, 256),
+    MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 256, 64),
+    MSHIFT_VARIANT(F16, MSHIFT_F16, 128, 128),
+    MSHIFT_VARIANT(F16, MSHIFT_F16, 64, 64),
+    MSHIFT_VARIANT(F16, MSHIFT_F16, 256, 256),
+    MSHIFT_VARIANT(F32, MSHIFT_F32, 128, 128),
+    MSHIFT_VARIANT(E4m3, MSHIFT_E4M3, 128, 128),
+    MSHIFT_VARIANT(E4m3, MSHIFT_E4M3, 256, 256),
+};
+constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+
+const Variant* find_variant(int32_t dtype, int32_t head_size, int32_t rotary, bool save) {
+  for (const Variant& v : kVariants) {
+    if (v.dtype != dtype || v.head_size != head_size) continue;
+    if (save || v.rotary == rotary) return &v;
+  }
+  return nullptr;
+}
+
+thread_local char g_cuda_error[256] = "";
+
+int cuda_fail(cudaError_t e) {
+  std::snprintf(g_cuda_error, sizeof(g_cuda_error), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return MSHIFT_ECUDA;
+}
+
+// Persistent grid: SMs x resident CTAs of this kernel, cached per device.
+struct GridCache {
+  std::mutex mu;
+  int sms[kMaxDevices] = {0};
+  int occ[kMaxDevices][2 * kNumVariants] = {{0}};
+};
+GridCache g_grid;
+
+int grid_for(KernelFn fn, int variant_slot, int64_t total, int* grid) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return MSHIFT_EINVAL;
+  std::lock_guard<std::mutex> lock(g_grid.mu);
+  if (g_grid.sms[dev] == 0) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_grid.sms[dev] = sms;
+  }
+  int& occ = g_grid.occ[dev][variant_slot];
+  if (occ == 0) {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (occ < 1) occ = 1;
+  }
+  const int64_t cap = (int64_t)g_grid.sms[dev] * occ;
+  *grid = static_cast<int>(total < cap ? total : cap);
+  return MSHIFT_OK;
+}
+
+int check_paged(const mshift_paged* p) {
+  if (p == nullptr) return MSHIFT_EINVAL;
+  if (p->block_size <= 0 || p->heads <= 0 || p->head_size <= 0 || p->num_blocks < 0)
+    return MSHIFT_EINVAL;
+  if (p->blk_stride < 0 || p->off_stride < 0 || p->head_stride < 0) return MSHIFT_EINVAL;
+  return MSHIFT_OK;
+}
+
+int elem_bytes(int32_t dtype) {
+  switch (dtype) {
+    case MSHIFT_BF16: case MSHIFT_F16: return 2;
+    case MSHIFT_F32: return 4;
+    case MSHIFT_E4M3: return 1;
+    default: return 0;
+  }
+}
+
+bool strides_aligned(int es, std::initializer_list<int64_t> strides) {
+  for (int64_t s : strides)
+    if ((s * es) % 16 != 0) return false;
+  return true;
+}
+
+int launch(KernelFn fn, int slot, const KArgs& args, cudaStream_t stream) {
+  const int64_t total = (int64_t)args.tiles_per_layer * args.n_layers;
+  if (total <= 0) return MSHIFT_OK;
+  int grid = 0;
+  int st = grid_for(fn, slot, total, &grid);
+  if (st != MSHIFT_OK) return st;
+  fn<<<grid, kThreads, 0, stream>>>(args);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
+}
+
+int variant_slot(const Variant* v, bool save) {
+  return static_cast<int>(v - kVariants) * 2 + (save ? 1 : 0);
+}
+
+int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_run* runs,
+            int32_t n_runs, int32_t tile_tokens, int32_t tiles_per_layer, int32_t n_layers,
+            void* const* store_ptrs, const int64_t* store_caps, int32_t n_sessions, int64_t st_tok,
+            int64_t st_head, void* const* k_ptrs, void* const* v_ptrs, const float* tables,
+            int32_t n_tables, const float* k_scales, uint32_t* err, void* stream) {
+  int st = check_paged(paged);
+  if (st != MSHIFT_OK) return st;
+  if (runs == nullptr || n_runs <= 0 || n_layers <= 0 || tiles_per_layer <= 0) return MSHIFT_EINVAL;
+  if (tile_tokens <= 0 || tile_tokens > kMaxTile) return MSHIFT_EINVAL;
+  if ((int64_t)tiles_per_layer * n_layers > INT32_MAX) return MSHIFT_EINVAL;
+  if (store_ptrs == nullptr || store_caps == nullptr || n_sessions <= 0) return MSHIFT_EINVAL;
+  if (k_ptrs == nullptr || v_ptrs == nullptr || err == nullptr) return MSHIFT_EINVAL;
+  if (st_tok < 0 || st_head < 0) return MSHIFT_EINVAL;
+  const int es = elem_bytes(paged->dtype);
+  if (es == 0) return MSHIFT_EUNSUPPORTED;
+  if (!strides_aligned(es, {paged->blk_stride, paged->off_stride, paged->head_stride, st_tok, st_head}))
+    return MSHIFT_EINVAL;
+  const Variant* v = find_variant(paged->dtype, paged->head_size, rotary, save);
+  if (v == nullptr) return MSHIFT_EUNSUPPORTED;
+  if (!save) {
+    if (n_tables > 0 && tables == nullptr) return MSHIFT_EINVAL;
+    if (paged->dtype == MSHIFT_E4M3 && k_scales == nullptr) return MSHIFT_EINVAL;
+  }
+  KArgs a{};
+  a.runs = runs;
+  a.n_runs = n_runs;
+  a.tile_tokens = tile_tokens;
+  a.tiles_per_layer = tiles_per_layer;
+  a.n_layers = n_layers;
+  a.store_ptrs = store_ptrs;
+  a.store_caps = store_caps;
+  a.n_sessions = n_sessions;
+  a.block_size = paged->block_size;
+  a.st_tok = st_tok;
+  a.st_head = st_head;
+  a.k_ptrs = k_ptrs;
+  a.v_ptrs = v_ptrs;
+  a.blk_stride = paged->blk_stride;
+  a.off_stride = paged->off_stride;
+  a.head_stride = paged->head_stride;
+  a.num_slots = paged->num_blocks * paged->block_size;
+  a.heads = paged->heads;
+  a.n_tables = save ? 0 : n_tables;
+  a.tables = save ? nullptr : tables;
+  a.k_scales = save ? nullptr : k_scales;
+  a.err = err;
+  return launch(save ? v->save : v->load, variant_slot(v, save), a,
+                static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace mshift
+
+// ====================================================================== C ABI
+using namespace mshift;
+
+extern "C" {
+
+int mshift_rope_tables(const int64_t* deltas, int32_t n, const float* inv_freq, int32_t half,
+                       float* tables, void* stream) {
+  if (n < 0 || half < 0) return MSHIFT_EINVAL;
+  if (n == 0 || half == 0) return MSHIFT_OK;
+  if (deltas == nullptr || inv_freq == nullptr || tables == nullptr) return MSHIFT_EINVAL;
+  const int64_t total = (int64_t)n * half;
+  const int threads = 128;
+  const int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > INT32_MAX) return MSHIFT_EINVAL;
+  rope_tables_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                       static_cast<cudaStream_t>(stream)>>>(deltas, n, inv_freq, half, tables);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
+}
+
+int mshift_scatter_shifted(const void* src, int64_t src_tok_stride, int64_t src_head_stride,
+                           int64_t n, void* k_base, void* v_base, const mshift_paged* paged,
+                           const int64_t* slots, const float* table, int32_t rotary,
+                           const float* k_scale, uint32_t* err, void* stream) {
+  int st = check_paged(paged);
+  if (st != MSHIFT_OK) return st;
+  if (n < 0) return MSHIFT_EINVAL;
+  if (n == 0) return MSHIFT_OK;  // zero-length load: nothing to do (shift_kernels.py:185-186)
+  if (n > INT32_MAX) return MSHIFT_EINVAL;
+  if (src == nullptr || k_base == nullptr || v_base == nullptr || slots == nullptr || err == nullptr)
+    return MSHIFT_EINVAL;
+  if (src_tok_stride < 0 || src_head_stride < 0) return MSHIFT_EINVAL;
+  const int es = elem_bytes(paged->dtype);
+  if (es == 0) return MSHIFT_EUNSUPPORTED;
+  if (!strides_aligned(es, {paged->blk_stride, paged->off_stride, paged->head_stride,
+                            src_tok_stride, src_head_stride}))
+    return MSHIFT_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(k_base) |
+       reinterpret_cast<uintptr_t>(v_base)) & 15u)
+    return MSHIFT_EINVAL;
+  const Variant* v = find_variant(paged->dtype, paged->head_size, rotary, false);
+  if (v == nullptr) return MSHIFT_EUNSUPPORTED;
+  if (table != nullptr && paged->dtype == MSHIFT_E4M3 && k_scale == nullptr) return MSHIFT_EINVAL;
+  const int32_t tt = mshift_default_tile_tokens(paged->heads);
+  KArgs a{};
+  a.runs = nullptr;
+  a.n_runs = 1;
+  a.tile_tokens = tt;
+  a.tiles_per_layer = static_cast<int32_t>((n + tt - 1) / tt);
+  a.n_layers = 1;
+  a.n_sessions = 1;
+  a.block_size = paged->block_size;
+  a.st_tok = src_tok_stride;
+  a.st_head = src_head_stride;
+  a.blk_stride = paged->blk_stride;
+  a.off_stride = paged->off_stride;
+  a.head_stride = paged->head_stride;
+  a.num_slots = paged->num_blocks * paged->block_size;
+  a.heads = paged->heads;
+  a.k_scales = k_scale;
+  a.err = err;
+  a.run0 = mshift_run{};
+  a.run0.store_start = 0;
+  a.run0.slots = slots;
+  a.run0.len = static_cast<int32_t>(n);
+  a.run0.table = table != nullptr ? 0 : -1;
+  a.run0.tile_begin = 0;
+  a.store0 = const_cast<void*>(src);
+  a.cap0 = n;
+  a.k0 = k_base;
+  a.v0 = v_base;
+  a.table0 = table;
+  return launch(v->load, variant_slot(v, false), a, static_cast<cudaStream_t>(stream));
+}
+
+int mshift_load(const mshift_paged* paged, int32_t rotary, const mshift_run* runs, int32_t n_runs,
+                int32_t tile_tokens, int32_t tiles_per_layer, int32_t n_layers,
+                void* const* store_ptrs, const int64_t* store_caps, int32_t n_sessions,
+                int64_t st_tok, int64_t st_head, void* const* k_ptrs, void* const* v_ptrs,
+                const float* tables, int32_t n_tables, const float* k_scales, uint32_t* err,
+                void* stream) {
+  return batched(false, paged, rotary, runs, n_runs, tile_tokens, tiles_per_layer, n_layers,
+                 store_ptrs, store_caps, n_sessions, st_tok, st_head, k_ptrs, v_ptrs, tables,
+                 n_tables, k_scales, err, stream);
+}
+
+int mshift_save(const mshift_paged* paged, const mshift_run* runs, int32_t n_runs,
+                int32_t tile_tokens, int32_t tiles_per_layer, int32_t n_layers,
+                void* const* store_ptrs, const int64_t* store_caps, int32_t n_sessions,
+                int64_t st_tok, int64_t st_head, void* const* k_ptrs, void* const* v_ptrs,
+                uint32_t* err, void* stream) {
+  return batched(true, paged, paged ? paged->head_size : 0, runs, n_runs, tile_tokens,
+                 tiles_per_layer, n_layers, store_ptrs, store_caps, n_sessions, st_tok, st_head,
+                 k_ptrs, v_ptrs, nullptr, 0, nullptr, err, stream);
+}
+
+int32_t mshift_plan_tiles(mshift_run* runs, int32_t n_runs, int32_t tile_tokens) {
+  if (runs == nullptr || n_runs <= 0 || tile_tokens <= 0) return -1;
+  int64_t acc = 0;
+  for (int32_t i = 0; i < n_runs; ++i) {
+    if (runs[i].len <= 0) return -1;
+    runs[i].tile_begin = static_cast<int32_t>(acc);
+    acc += (runs[i].len + tile_tokens - 1) / tile_tokens;
+    if (acc > INT32_MAX) return -1;
+  }
+  return static_cast<int32_t>(acc);
+}
+
+int32_t mshift_default_tile_tokens(int32_t heads) {
+  if (heads <= 0) return 16;
+  int32_t t = 256 / heads;
+  if (t < 16) t = 16;
+  if (t > kMaxTile) t = kMaxTile;
+  return t;
+}
+
+int mshift_supported(int32_t dtype, int32_t head_size, int32_t rotary) {
+  return find_variant(dtype, head_size, rotary, false) != nullptr ? 1 : 0;
+}
+
+const char* mshift_version(void) { return "marathon_b200 shift 0.1 (sm_100a)"; }
+
+const char* mshift_strerror(int status) {
+  switch (status) {
+    case MSHIFT_OK: return "ok";
+    case MSHIFT_EINVAL: return "invalid argument";
+    case MSHIFT_EUNSUPPORTED: return "unsupported dtype / head_size / rotary combination";
+    case MSHIFT_ECUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+const char* mshift_last_cuda_error(void) { return g_cuda_error; }
+
+}  // extern "C"

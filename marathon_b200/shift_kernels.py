@@ -1,0 +1,573 @@
+"""Re-rotate-and-scatter (load) and paged gather (save) on B200, behind the reference API.
+
+Drop-in surface of the reference's ``marathon.shift_kernels``
+(``src/marathon/shift_kernels.py``):
+
+* :class:`RopeShift` / :func:`rope_shift` — per-delta rotation tables
+  (``:50-84``).  The kernel reads one ``[2, rotary/2]`` fp32 table (cos, sin);
+  the reference's ``cos``/``sgn``/``partner``/``emb_cos``/``emb_sin`` views
+  are kept on the object for callers that use them.
+* :func:`scatter_shifted` — one layer, one run (``:166-210``).
+* :func:`warmup` — the reference pre-compiled Triton here (``:213-238``); the
+  sm_100a kernels are compiled ahead of time, so this only loads the library
+  and resolves the launch grid.
+
+plus the batched entry points the connector uses, :class:`Launcher.load` and
+:class:`Launcher.save`, which run every run x every layer x every session of a
+step in one persistent launch each.
+
+There is no CPU path: a CPU tensor, a missing library or a non-zero native
+status raises :class:`ShiftError`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import RUN_DTYPE, ShiftError
+from .paged import KVLayers, PagedLayout, describe, paged_strides
+
+__all__ = [
+    "RopeShift",
+    "rope_shift",
+    "rope_tables",
+    "scatter_shifted",
+    "warmup",
+    "inv_freq",
+    "RunSpec",
+    "StoreView",
+    "Launcher",
+    "ShiftError",
+    "paged_strides",
+]
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ShiftError(
+            f"{what} is on {t.device}: the shift kernels are CUDA-only and have no CPU path"
+        )
+
+
+def inv_freq(rotary: int, theta: float) -> torch.Tensor:
+    """RoPE inverse frequencies exactly as the connector forms them (fp32, on CPU).
+
+    ``1 / theta ** (arange(0, rotary, 2) / rotary)``
+    (``src/marathon/vllm_shift_connector.py:196-198``).
+    """
+    return 1.0 / (theta ** (torch.arange(0, rotary, 2, dtype=torch.float32) / rotary))
+
+
+# ------------------------------------------------------------------ tables
+@dataclass(frozen=True)
+class RopeShift:
+    """Rotation tables of one delta on the device the kernel runs on.
+
+    ``table`` (``[2, rotary/2]``: cos then sin of ``fp32(delta) * inv_freq``) is
+    what the kernel reads.  ``cos``/``sgn``/``partner``/``emb_cos``/``emb_sin``
+    are the reference's branchless and broadcast forms of the same numbers
+    (``src/marathon/shift_kernels.py:50-65``): ``out[i] = k[i]*cos[i] +
+    k[partner[i]]*sgn[i]``, with a non-rotary tail of ``cos = 1, sgn = 0``.
+    """
+
+    delta: int
+    cos: torch.Tensor
+    sgn: torch.Tensor
+    partner: torch.Tensor
+    emb_cos: torch.Tensor
+    emb_sin: torch.Tensor
+    table: torch.Tensor = field(repr=False)
+
+    @property
+    def rotary(self) -> int:
+        return int(self.emb_cos.numel())
+
+
+def rope_tables(deltas: torch.Tensor, inv: torch.Tensor) -> torch.Tensor:
+    """``[n, 2, half]`` cos/sin tables for ``n`` deltas in one launch (device tensors)."""
+    _require_cuda(deltas, "deltas")
+    _require_cuda(inv, "inv_freq")
+    deltas = deltas.to(torch.int64).contiguous()
+    inv = inv.to(torch.float32).contiguous()
+    half = int(inv.numel())
+    out = torch.empty((deltas.numel(), 2, half), dtype=torch.float32, device=deltas.device)
+    lib = _lib.load()
+    _lib.check(
+        lib.mshift_rope_tables(
+            deltas.data_ptr(), deltas.numel(), inv.data_ptr(), half, out.data_ptr(),
+            _stream_ptr(deltas.device),
+        ),
+        "mshift_rope_tables",
+    )
+    return out
+
+
+def rope_shift(delta: int, head_size: int, inv_freq: torch.Tensor, device) -> RopeShift:
+    """Tables that move RoPE'd keys ``delta`` positions, for one head dimension.
+
+    Same signature and fields as the reference (``shift_kernels.py:68-84``);
+    the numbers come from the native table kernel.
+    """
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise ShiftError("rope_shift builds its tables with a CUDA kernel; pass a CUDA device")
+    rotary = 2 * int(inv_freq.numel())
+    if rotary > head_size:
+        raise ShiftError(f"rotary {rotary} > head_size {head_size}")
+    half = rotary // 2
+    inv = inv_freq.to(device=device, dtype=torch.float32)
+    table = rope_tables(torch.tensor([int(delta)], dtype=torch.int64, device=device), inv)[0]
+    c, s = table[0], table[1]
+    cos = torch.ones(head_size, dtype=torch.float32, device=device)
+    sgn = torch.zeros(head_size, dtype=torch.float32, device=device)
+    cos[:rotary] = torch.cat((c, c))
+    sgn[:half] = -s
+    sgn[half:rotary] = s
+    partner = torch.arange(head_size, dtype=torch.int32, device=device)
+    partner[:half] += half
+    partner[half:rotary] -= half
+    return RopeShift(int(delta), cos, sgn, partner, torch.cat((c, c)), torch.cat((s, s)), table)
+
+
+# ------------------------------------------------------------ error words
+_ERR: dict[int, torch.Tensor] = {}
+
+
+def _err_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ERR.get(idx)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=device)
+        _ERR[idx] = t
+    return t
+
+
+def take_errors(device=None) -> int:
+    """Synchronise, return and clear the error bits accumulated by unchecked launches."""
+    device = torch.device(device if device is not None else "cuda")
+    t = _err_word(device)
+    bits = int(t[0].item())
+    t.zero_()
+    return bits
+
+
+def _raise_bits(bits: int, what: str) -> None:
+    if bits:
+        raise ShiftError(f"{what}: kernel rejected tokens ({_lib.describe_bits(bits)}); "
+                         "those tokens were not written")
+
+
+# ------------------------------------------------------------ single layer
+def scatter_shifted(
+    src: torch.Tensor,
+    kv: torch.Tensor,
+    slots: torch.Tensor,
+    block_size: int,
+    hnd: bool,
+    shift: RopeShift | None,
+    *,
+    k_scale: torch.Tensor | None = None,
+    fp8: bool = False,
+    check: bool = False,
+) -> None:
+    """Write ``src`` (``[n, heads, 2*head_size]``) into ``kv``'s slots, K rotated by delta.
+
+    Contract of the reference (``shift_kernels.py:166-210``): ``slots`` are
+    flat destination slots (block ``slot // block_size``, offset
+    ``slot % block_size``), ``hnd`` selects the fused layout, ``shift=None`` or
+    delta 0 is a plain scatter, ``n == 0`` is a no-op.  ``src`` must have the
+    cache's dtype (the store holds cache-dtype rows).  E4M3 caches
+    (``float8_e4m3fn``, or ``uint8`` with ``fp8=True``) need ``k_scale``, a
+    one-element fp32 device tensor.  ``check=True`` synchronises and raises on
+    any token the kernel rejected; otherwise rejections accumulate for
+    :func:`take_errors`.
+    """
+    _require_cuda(kv, "kv")
+    n, heads, two_d = src.shape
+    if kv.shape[-1] != two_d:
+        raise ShiftError(f"src row {two_d} != kv row {kv.shape[-1]}")
+    if n == 0:
+        return
+    _require_cuda(src, "src")
+    _require_cuda(slots, "slots")
+    if src.dtype != kv.dtype:
+        raise ShiftError(f"src dtype {src.dtype} != cache dtype {kv.dtype}")
+    if src.stride(-1) != 1:
+        raise ShiftError("src rows must be contiguous in the head dimension")
+    geo = describe(kv, block_size, "hnd" if hnd else "nhd", fp8=fp8)
+    if geo.heads != heads:
+        raise ShiftError(f"src has {heads} heads, cache has {geo.heads}")
+    slots = slots.to(torch.int64).contiguous()
+    if slots.numel() != n:
+        raise ShiftError(f"{slots.numel()} slots for {n} tokens")
+    rotate = shift is not None and shift.delta != 0
+    rotary = shift.rotary if shift is not None else geo.head_size
+    table_ptr = shift.table.data_ptr() if rotate else None
+    ks_ptr = None
+    if geo.dtype == _lib.E4M3 and rotate:
+        if k_scale is None:
+            raise ShiftError("an e4m3 cache needs k_scale to re-rotate keys")
+        k_scale = k_scale.to(device=kv.device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+        ks_ptr = k_scale.data_ptr()
+    err = _err_word(kv.device)
+    k_base = kv.data_ptr()
+    v_base = k_base + geo.head_size * geo.elem_bytes
+    lib = _lib.load()
+    paged = geo.struct()
+    _lib.check(
+        lib.mshift_scatter_shifted(
+            src.data_ptr(), src.stride(0), src.stride(1), n, k_base, v_base,
+            ctypes.byref(paged), slots.data_ptr(), table_ptr, rotary, ks_ptr,
+            err.data_ptr(), _stream_ptr(kv.device),
+        ),
+        "mshift_scatter_shifted",
+    )
+    if check:
+        _raise_bits(take_errors(kv.device), "scatter_shifted")
+
+
+def warmup(kv: torch.Tensor, block_size: int, hnd: bool) -> None:
+    """Load the library and validate ``kv``'s geometry before the first real load.
+
+    The reference JIT-compiled Triton here (``shift_kernels.py:213-238``); the
+    native kernels are compiled ahead of time, so nothing is compiled.
+    """
+    lib = _lib.load()
+    if not kv.is_cuda:
+        return
+    geo = describe(kv, block_size, "hnd" if hnd else "nhd")
+    if not lib.mshift_supported(geo.dtype, geo.head_size, geo.head_size):
+        raise ShiftError(f"no kernel for dtype code {geo.dtype}, head_size {geo.head_size}")
+
+
+# ------------------------------------------------------------------ batches
+@dataclass
+class RunSpec:
+    """One run of a batch: ``length`` tokens of ``session`` starting at ``store_start``.
+
+    The paged side is ``slots`` (CUDA int64 ``[length]``, the reference's
+    ``_Load.slots``) or ``block_table`` plus ``paged_start`` (the logical
+    position of the first token).  A ``block_table`` given as a host sequence
+    or numpy array travels to the device inside the batch's single descriptor
+    copy; a CUDA int32 tensor is used in place.  ``delta`` is the RoPE offset
+    of a load (ignored by saves).
+    """
+
+    session: int
+    store_start: int
+    length: int
+    delta: int = 0
+    slots: torch.Tensor | None = None
+    block_table: object = None
+    paged_start: int = 0
+
+
+@dataclass
+class StoreView:
+    """Store buffers of the sessions in a batch, indexed [session row][layer]."""
+
+    ptrs: np.ndarray  # uint64 [n_sessions, n_layers]; 0 = missing buffer
+    caps: np.ndarray  # int64 [n_sessions]
+    st_tok: int
+    st_head: int
+    keepalive: list = field(default_factory=list, repr=False)
+
+
+def _align(n: int, a: int = 16) -> int:
+    return (n + a - 1) // a * a
+
+
+class _Staging:
+    """Pinned host + device staging of one batch's descriptors, double-buffered.
+
+    A batch's descriptors — run records, store pointer table, capacities,
+    deltas, host block tables and a zeroed error word — reach the device in
+    ONE host-to-device copy.  Two slots alternate so the next batch can be
+    packed while the previous batch's kernels still read theirs.
+    """
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.cap = 0
+        self.host: list[torch.Tensor] = []
+        self.dev: list[torch.Tensor] = []
+        self.done: list[torch.cuda.Event | None] = [None, None]
+        self.slot = 0
+        self.err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def _ensure(self, n: int) -> None:
+        if n <= self.cap:
+            return
+        for ev in self.done:
+            if ev is not None:
+                ev.synchronize()
+        cap = 1 << max(12, (n - 1).bit_length())
+        self.host = [torch.empty(cap, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.dev = [torch.empty(cap, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        self.done = [None, None]
+        self.cap = cap
+
+    def begin(self, n: int) -> tuple[int, np.ndarray, int]:
+        """Pick a free slot: (slot, host bytes view, device base address)."""
+        self._ensure(n)
+        slot = self.slot
+        self.slot ^= 1
+        ev = self.done[slot]
+        if ev is not None:
+            ev.synchronize()
+        return slot, self.host[slot].numpy(), self.dev[slot].data_ptr()
+
+    def upload(self, slot: int, n: int) -> None:
+        self.dev[slot][:n].copy_(self.host[slot][:n], non_blocking=True)
+
+    def finish(self, slot: int, stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.done[slot] = ev
+
+    def read_err(self, slot: int, stream) -> int:
+        self.err_host.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
+        stream.synchronize()
+        return int(self.err_host[0])
+
+
+@dataclass
+class Prepared:
+    """A staged batch: descriptors on the device, ready to launch."""
+
+    kind: str  # "load" | "save"
+    slot: int
+    base: int  # device address of the staging slot (error word at +0)
+    runs: int
+    n_runs: int
+    tiles: int
+    n_layers: int
+    first_layer: int
+    ptrs: int
+    caps: int
+    n_sessions: int
+    st_tok: int
+    st_head: int
+    deltas: int
+    n_deltas: int
+    h2d_bytes: int
+    tables: torch.Tensor | None = None
+    k_scales: torch.Tensor | None = None
+    inv_freq: torch.Tensor | None = None
+
+
+class Launcher:
+    """Batched load/save over registered paged caches, one persistent launch per call.
+
+    ``layers`` is the :class:`KVLayers` of this rank's caches.  ``load`` /
+    ``save`` = :meth:`prepare_load` / :meth:`prepare_save` (pack on the host,
+    one H2D copy) + :meth:`launch` (native calls only) + an optional error
+    check (one 4-byte D2H read and a stream sync).
+    """
+
+    def __init__(self, layers: KVLayers, tile_tokens: int | None = None) -> None:
+        if layers.k_ptrs is None:
+            raise ShiftError("the batched kernels need CUDA caches")
+        self.layers = layers
+        self.geo: PagedLayout = layers.geometry
+        self.device = layers.device
+        self.lib = _lib.load()
+        self.tile_tokens = int(tile_tokens or self.lib.mshift_default_tile_tokens(self.geo.heads))
+        self.paged = self.geo.struct()
+        self.staging = _Staging(self.device)
+        self.last_launches = 0
+        self.last_h2d = 0  # bytes of the last batch's descriptor copy
+
+    # -- packing ------------------------------------------------------------
+    def _prepare(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
+        n_runs = len(runs)
+        S, L = store.ptrs.shape
+        if L != n_layers:
+            raise ShiftError(f"store view has {L} layers, the launch covers {n_layers}")
+        host_tables: list[tuple[int, np.ndarray]] = []
+        for i, r in enumerate(runs):
+            if r.slots is None and r.block_table is not None and not isinstance(
+                r.block_table, torch.Tensor
+            ):
+                host_tables.append((i, np.ascontiguousarray(r.block_table, dtype=np.int32)))
+        o_runs = 16
+        o_ptrs = _align(o_runs + RUN_DTYPE.itemsize * n_runs)
+        o_caps = _align(o_ptrs + 8 * S * L)
+        o_deltas = _align(o_caps + 8 * S)
+        o_tabs = _align(o_deltas + 8 * max(len(deltas), 1))
+        tab_at, at = {}, o_tabs
+        for i, bt in host_tables:
+            tab_at[i] = at
+            at = _align(at + bt.nbytes)
+        total = at
+
+        slot, host, base = self.staging.begin(total)
+        rec = np.zeros(n_runs, dtype=RUN_DTYPE)
+        tiles = 0
+        tt = self.tile_tokens
+        table_of = {d: i for i, d in enumerate(deltas)}
+        for i, r in enumerate(runs):
+            if r.length <= 0:
+                raise ShiftError(f"run {i} has length {r.length}")
+            if not 0 <= r.session < S:
+                raise ShiftError(f"run {i} names session row {r.session} of {S}")
+            rec[i]["store_start"] = r.store_start
+            rec[i]["len"] = r.length
+            rec[i]["session"] = r.session
+            rec[i]["table"] = table_of[int(r.delta)] if int(r.delta) in table_of else -1
+            rec[i]["tile_begin"] = tiles
+            tiles += -(-r.length // tt)
+            if r.slots is not None:
+                if r.slots.dtype != torch.int64 or not r.slots.is_cuda or r.slots.numel() < r.length:
+                    raise ShiftError(f"run {i}: slots must be a CUDA int64 tensor of >= {r.length}")
+                rec[i]["slots"] = r.slots.data_ptr()
+            elif r.block_table is not None:
+                if isinstance(r.block_table, torch.Tensor):
+                    if r.block_table.dtype != torch.int32 or not r.block_table.is_cuda:
+                        raise ShiftError(f"run {i}: a tensor block_table must be CUDA int32")
+                    rec[i]["block_table"] = r.block_table.data_ptr()
+                    rec[i]["block_table_len"] = r.block_table.numel()
+                else:
+                    rec[i]["block_table"] = base + tab_at[i]
+                    rec[i]["block_table_len"] = len(r.block_table)
+                rec[i]["paged_start"] = r.paged_start
+            else:
+                raise ShiftError(f"run {i} has neither slots nor a block table")
+        if tiles * n_layers > 2**31 - 1:
+            raise ShiftError("batch too large for one launch")
+
+        host[:16] = 0  # the error word
+        host[o_runs : o_runs + rec.nbytes] = rec.view(np.uint8)
+        host[o_ptrs : o_ptrs + 8 * S * L] = (
+            np.ascontiguousarray(store.ptrs, dtype=np.uint64).view(np.uint8).reshape(-1)
+        )
+        host[o_caps : o_caps + 8 * S] = np.ascontiguousarray(store.caps, dtype=np.int64).view(
+            np.uint8
+        )
+        if deltas:
+            host[o_deltas : o_deltas + 8 * len(deltas)] = np.asarray(deltas, dtype=np.int64).view(
+                np.uint8
+            )
+        for i, bt in host_tables:
+            host[tab_at[i] : tab_at[i] + bt.nbytes] = bt.view(np.uint8)
+        self.staging.upload(slot, total)
+        self.last_h2d = total
+        return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
+                        base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
+                        base + o_deltas, len(deltas), total)
+
+    def prepare_load(
+        self,
+        runs: list[RunSpec],
+        store: StoreView,
+        inv_freq: torch.Tensor,
+        *,
+        k_scales: torch.Tensor | None = None,
+    ) -> Prepared:
+        _require_cuda(inv_freq, "inv_freq")
+        deltas = sorted({int(r.delta) for r in runs if int(r.delta) != 0})
+        if self.geo.dtype == _lib.E4M3 and deltas:
+            if k_scales is None:
+                raise ShiftError("an e4m3 cache needs per-layer k_scales to re-rotate keys")
+            k_scales = k_scales.to(device=self.device, dtype=torch.float32).contiguous()
+            if k_scales.numel() < len(self.layers):
+                raise ShiftError("need one K scale per layer")
+        p = self._prepare("load", runs, store, deltas, 0, len(self.layers))
+        p.inv_freq = inv_freq.to(torch.float32).contiguous()
+        p.k_scales = k_scales if deltas else None
+        if deltas:
+            p.tables = torch.empty((len(deltas), 2, p.inv_freq.numel()), dtype=torch.float32,
+                                   device=self.device)
+        return p
+
+    def prepare_save(
+        self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
+        n_layers: int | None = None,
+    ) -> Prepared:
+        n_layers = len(self.layers) - first_layer if n_layers is None else int(n_layers)
+        if first_layer < 0 or n_layers <= 0 or first_layer + n_layers > len(self.layers):
+            raise ShiftError(f"layer range [{first_layer}, +{n_layers}) outside the caches")
+        return self._prepare("save", runs, store, [], first_layer, n_layers)
+
+    def launch(self, p: Prepared, *, tables: bool = True, main: bool = True) -> int:
+        """Issue the native launches of a prepared batch; returns how many were issued."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        n = 0
+        if p.kind == "load":
+            half = int(p.inv_freq.numel())
+            if tables and p.n_deltas:
+                _lib.check(
+                    self.lib.mshift_rope_tables(p.deltas, p.n_deltas, p.inv_freq.data_ptr(), half,
+                                                p.tables.data_ptr(), stream),
+                    "mshift_rope_tables",
+                )
+                n += 1
+            if main:
+                _lib.check(
+                    self.lib.mshift_load(
+                        ctypes.byref(self.paged), 2 * half, p.runs, p.n_runs, self.tile_tokens,
+                        p.tiles, p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
+                        self.layers.k_ptrs.data_ptr(), self.layers.v_ptrs.data_ptr(),
+                        p.tables.data_ptr() if p.tables is not None else None, p.n_deltas,
+                        p.k_scales.data_ptr() if p.k_scales is not None else None, p.base,
+                        stream,
+                    ),
+                    "mshift_load",
+                )
+                n += 1
+        else:
+            if main:
+                off = 8 * p.first_layer
+                _lib.check(
+                    self.lib.mshift_save(
+                        ctypes.byref(self.paged), p.runs, p.n_runs, self.tile_tokens, p.tiles,
+                        p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
+                        self.layers.k_ptrs.data_ptr() + off, self.layers.v_ptrs.data_ptr() + off,
+                        p.base, stream,
+                    ),
+                    "mshift_save",
+                )
+                n += 1
+        self.last_launches = n
+        return n
+
+    def finish(self, p: Prepared, check: bool) -> None:
+        stream = torch.cuda.current_stream(self.device)
+        self.staging.finish(p.slot, stream)
+        if check:
+            _raise_bits(self.staging.read_err(p.slot, stream), f"shift {p.kind}")
+
+    # -- one-call entry points ---------------------------------------------
+    def load(self, runs: list[RunSpec], store: StoreView, inv_freq: torch.Tensor, *,
+             k_scales: torch.Tensor | None = None, check: bool = True) -> None:
+        """Every run x every layer: store rows -> paged cache, K rotated by its delta.
+
+        ``inv_freq`` is the fp32 device tensor of the RoPE inverse frequencies,
+        ``k_scales`` the per-layer fp32 K scales of an e4m3 cache.
+        """
+        if not runs:
+            return
+        p = self.prepare_load(runs, store, inv_freq, k_scales=k_scales)
+        self.launch(p)
+        self.finish(p, check)
+
+    def save(self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
+             n_layers: int | None = None, check: bool = True) -> None:
+        """Every run x layers ``[first_layer, +n_layers)``: paged rows -> store rows, bit copy.
+
+        ``store.ptrs`` has one column per layer of that range.
+        """
+        if not runs:
+            return
+        p = self.prepare_save(runs, store, first_layer=first_layer, n_layers=n_layers)
+        self.launch(p)
+        self.finish(p, check)

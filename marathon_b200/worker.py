@@ -1,0 +1,174 @@
+"""Worker side of the shift connector, independent of vLLM's plumbing.
+
+:class:`ShiftWorker` is what ``MarathonShiftConnector`` runs on a worker: it
+holds the registered paged caches and the session store, and turns one step's
+loads (or saves) into ONE native launch over every load x every layer.  The
+reference ran one Triton launch per layer per load, preceded by a
+``ShiftStore.read`` and a slot transfer per layer
+(``src/marathon/vllm_shift_connector.py:495-518``); here the decisions are the
+same (``ShiftStore`` bookkeeping, counters and LRU touches per layer) but the
+bytes move in a single persistent kernel, and the request's block table rides
+to the device inside the batch's single descriptor copy instead of a per-token
+slot tensor.
+"""
+
+from __future__ import annotations
+
+import logging
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .paged import KVLayers
+from .shift_kernels import Launcher, RunSpec, ShiftError
+from .shift_store import ShiftStore, slots as host_slots
+
+logger = logging.getLogger("vllm.marathon_shift")
+
+
+@dataclass
+class LoadJob:
+    """One load: store ``[src_start, +length)`` -> logical ``[dst_start, +length)``."""
+
+    session: str
+    src_start: int
+    delta: int
+    dst_start: int
+    length: int
+    block_ids: list[int] | np.ndarray | None = None
+    slots: torch.Tensor | None = None  # alternative to block_ids: flat slots
+
+    def host_slots(self, block_size: int) -> torch.Tensor:
+        if self.slots is not None:
+            return self.slots.cpu()
+        return host_slots(list(self.block_ids), self.dst_start, self.dst_start + self.length,
+                          block_size)
+
+
+@dataclass
+class SaveJob:
+    """One save: logical positions ``[dst_start, +length)`` -> the same store rows."""
+
+    session: str
+    dst_start: int
+    length: int
+    block_ids: list[int] | np.ndarray | None = None
+    slots: torch.Tensor | None = None
+
+
+def _run(row: int, store_start: int, length: int, delta: int, block_ids, slots, paged_start):
+    if slots is not None:
+        return RunSpec(row, store_start, length, delta, slots=slots)
+    return RunSpec(row, store_start, length, delta, block_table=np.asarray(block_ids, np.int32),
+                   paged_start=paged_start)
+
+
+class ShiftWorker:
+    """Registered caches + store; batched native load and save."""
+
+    def __init__(
+        self,
+        store: ShiftStore,
+        block_size: int,
+        inv_freq: torch.Tensor,
+        *,
+        layout: str | None = None,
+        fp8: bool = False,
+        k_scales: torch.Tensor | None = None,
+    ) -> None:
+        self.store = store
+        self.block_size = int(block_size)
+        self.inv_cpu = inv_freq.to(torch.float32)
+        self.layout = layout
+        self.fp8 = fp8
+        self.k_scales = k_scales
+        self.layers: KVLayers | None = None
+        self.launcher: Launcher | None = None
+        self.inv: torch.Tensor | None = None
+
+    @property
+    def registered(self) -> bool:
+        return self.layers is not None
+
+    def register(self, kv_caches: dict[str, torch.Tensor]) -> KVLayers:
+        self.layers = KVLayers(kv_caches, self.block_size, self.layout, fp8=self.fp8)
+        self.launcher = Launcher(self.layers)
+        self.inv = self.inv_cpu.to(self.layers.device)
+        if self.k_scales is not None:
+            self.k_scales = self.k_scales.to(self.layers.device, torch.float32)
+        return self.layers
+
+    # ---------------------------------------------------------------- load
+    def load(self, jobs: list[LoadJob], *, check: bool = True) -> list[LoadJob]:
+        """Every job x every layer in one launch.  Returns the jobs that were issued.
+
+        A job whose rows are not all held (evicted, truncated, a layer never
+        saved) stops the batch there, as the reference's load loop returned on
+        the first missing layer (``vllm_shift_connector.py:506-513``): jobs
+        before it are loaded, it and later ones are not.
+        """
+        if not jobs:
+            return []
+        if self.launcher is None:
+            raise ShiftError("no KV caches registered")
+        names = self.layers.names
+        accepted: list[LoadJob] = []
+        for job in jobs:
+            missing = self.store.loadable(job.session, names, job.src_start, job.length)
+            if missing is not None:
+                logger.error("shift: session %s has no stored KV for %s; load skipped",
+                             job.session, missing)
+                break
+            self.store.mark_loaded(job.session, names, job.length)
+            accepted.append(job)
+        if not accepted:
+            return []
+        rows: dict[str, int] = {}
+        runs = []
+        for job in accepted:
+            row = rows.setdefault(job.session, len(rows))
+            runs.append(_run(row, job.src_start, job.length, job.delta, job.block_ids, job.slots,
+                             job.dst_start))
+        view = self.store.view(list(rows), names)
+        self.launcher.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
+        return accepted
+
+    # ---------------------------------------------------------------- save
+    def save(self, jobs: list[SaveJob], layer_names: list[str] | None = None, *,
+             check: bool = True) -> int:
+        """Gather ``jobs`` out of the paged caches of ``layer_names`` into the store.
+
+        The layers must be consecutive in registration order (one launch covers
+        a contiguous range); the store rows must already be reserved.  Returns
+        the number of token-layers written.
+        """
+        if not jobs:
+            return 0
+        if self.launcher is None:
+            raise ShiftError("no KV caches registered")
+        names = layer_names if layer_names is not None else self.layers.names
+        idx = [self.layers.index[n] for n in names]
+        first = idx[0]
+        if idx != list(range(first, first + len(idx))):
+            raise ShiftError("a batched save covers consecutive layers only")
+        geo = self.layers.geometry
+        dtype = self.layers.tensors[0].dtype
+        rows: dict[str, int] = {}
+        runs = []
+        for job in jobs:
+            if not self.store.ensure_layers(job.session, names, geo.heads, 2 * geo.head_size,
+                                            dtype):
+                continue
+            if job.dst_start + job.length > self.store.capacity(job.session):
+                continue
+            row = rows.setdefault(job.session, len(rows))
+            runs.append(_run(row, job.dst_start, job.length, 0, job.block_ids, job.slots,
+                             job.dst_start))
+        if not runs:
+            return 0
+        view = self.store.view(list(rows), names)
+        self.launcher.save(runs, view, first_layer=first, n_layers=len(names), check=check)
+        done = sum(r.length for r in runs)
+        self.store.mark_saved(done, len(names))
+        return done * len(names)
