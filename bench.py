@@ -137,13 +137,6 @@ class Clocks:
         }
 
 
-def shard(heads: int, rank: int, world: int) -> tuple[int, int]:
-    if heads % world:
-        raise SystemExit(f"{heads} KV heads do not split over {world} ranks")
-    per = heads // world
-    return rank * per, (rank + 1) * per
-
-
 # --------------------------------------------------------- CPU baseline
 class CpuPath:
     """The reference's torch CPU path on two resident layers of ``cfg``'s first segment."""
@@ -241,6 +234,7 @@ def native_arm(args) -> None:
     import torch.distributed as dist
 
     from marathon_b200.paged import KVLayers
+    from marathon_b200.sharding import broadcast_table, head_shard, pack_table
     from marathon_b200.shift_kernels import Launcher
     from marathon_b200.shift_store import ShiftStore
     from marathon_b200.worker import LoadJob, ShiftWorker
@@ -255,7 +249,7 @@ def native_arm(args) -> None:
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
 
     cfg = config(args.config)
-    h_lo, h_hi = shard(cfg.heads, rank, world)
+    h_lo, h_hi = head_shard(cfg.heads, rank, world)
     wl = build(cfg, device, head_lo=h_lo, head_hi=h_hi, layout=args.layout)
     fp8 = cfg.dtype == "e4m3"
     layers = KVLayers(wl.kv, cfg.block_size, args.layout, fp8=fp8)
@@ -263,12 +257,10 @@ def native_arm(args) -> None:
     view = wl.store_view()
 
     # control plane: the segment table is rank 0's, broadcast once over NCCL
-    table = torch.tensor([[r.session, r.store_start, r.length, r.delta, r.paged_start]
-                          for r in wl.runs], dtype=torch.int64, device=device)
     if world > 1:
-        mine = table.clone()
-        dist.broadcast(table, src=0)
-        if not torch.equal(mine, table):
+        mine = pack_table(wl.runs)
+        got = broadcast_table(mine if rank == 0 else None, len(wl.runs), device=device)
+        if not torch.equal(mine, got.cpu()):
             raise SystemExit(f"rank {rank}: segment table differs from rank 0's")
 
     def step(check=False, ev=None):

@@ -1,0 +1,226 @@
+"""The vLLM connector: scheduler-side decisions on CPU, worker-side data path on the GPU.
+
+vLLM objects are faked with the handful of attributes the connector reads
+(the same fields the reference connector uses: ``req_id``, ``block_ids``,
+``num_computed_tokens``, ``num_scheduled_tokens``, ``finished_req_ids``).
+"""
+
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.base")
+KVConnectorRole = vllm_base.KVConnectorRole
+
+from marathon_b200 import gapfill  # noqa: E402
+from marathon_b200 import vllm_shift_connector as C  # noqa: E402
+
+BS = 16
+
+
+def fake_config(extra=None, head_dim=128, cache_dtype="auto"):
+    hf = SimpleNamespace(head_dim=head_dim, hidden_size=4096, num_attention_heads=32,
+                         partial_rotary_factor=1.0, rope_theta=1e6)
+    return SimpleNamespace(
+        kv_transfer_config=SimpleNamespace(kv_connector_extra_config=extra or {}),
+        cache_config=SimpleNamespace(block_size=BS, cache_dtype=cache_dtype),
+        model_config=SimpleNamespace(hf_text_config=hf),
+    )
+
+
+def request(rid, params, n_prompt):
+    return SimpleNamespace(request_id=rid, kv_transfer_params=params, num_prompt_tokens=n_prompt)
+
+
+def new_req(rid, blocks, computed):
+    return SimpleNamespace(req_id=rid, block_ids=(list(blocks),), num_computed_tokens=computed)
+
+
+def sched_output(new=(), cached=None, scheduled=None, finished=()):
+    cached = cached or SimpleNamespace(req_ids=[], new_block_ids=[], num_computed_tokens=[])
+    return SimpleNamespace(scheduled_new_reqs=list(new), scheduled_cached_reqs=cached,
+                           num_scheduled_tokens=dict(scheduled or {}),
+                           finished_req_ids=set(finished))
+
+
+def scheduler(extra=None):
+    return C.MarathonShiftConnector(fake_config(extra or {"store_tokens": 65536}),
+                                    KVConnectorRole.SCHEDULER, None)
+
+
+def test_inv_freq_and_theta_follow_the_model_config():
+    conn = scheduler()
+    want = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    assert torch.equal(conn._inv_freq, want)
+    cfg = fake_config()
+    del cfg.model_config.hf_text_config.rope_theta
+    cfg.model_config.hf_text_config.rope_parameters = {"rope_theta": 5e5}
+    c2 = C.MarathonShiftConnector(cfg, KVConnectorRole.SCHEDULER, None)
+    assert torch.equal(c2._inv_freq, 1.0 / (5e5 ** (torch.arange(0, 128, 2,
+                                                                   dtype=torch.float32) / 128)))
+
+
+def test_first_turn_saves_then_edit_turn_loads_shifted():
+    conn = scheduler()
+    # turn 0: 1000-token prompt, nothing to load, everything saved
+    r0 = request("r0", {"session": "s", "save": True}, 1000)
+    conn.on_new_request(r0)
+    assert conn.get_num_new_matched_tokens(r0, 0) == (0, False)
+    blocks0 = list(range(100, 100 + 63))
+    meta = conn.build_connector_meta(sched_output([new_req("r0", blocks0, 0)], scheduled={"r0": 1000}))
+    assert not meta.loads and len(meta.saves) == 1
+    sv = meta.saves[0]
+    assert (sv.session, sv.dst_start, sv.length) == ("s", 0, 1000)
+    assert sv.slots.tolist() == (np.asarray(blocks0)[np.arange(1000) // BS] * BS
+                                 + np.arange(1000) % BS).tolist()
+    conn.request_finished(r0, blocks0)
+
+    # turn 1: an edit at 200 grows 40 tokens by 24, the suffix [240, 1000) moves to [264, 1024)
+    load = {"dst_start": 264, "dst_end": 1024, "delta": 24}
+    r1 = request("r1", {"session": "s", "load": load, "save": "full"}, 1100)
+    conn.on_new_request(r1)
+    # vLLM's own prefix cache hit stops at 256 (block aligned, before the edit end)
+    n, async_ = conn.get_num_new_matched_tokens(r1, 264 - 264 % BS + BS)
+    assert async_ is False
+    lo, hi = 272, 1024
+    assert n == hi - lo
+    conn.update_state_after_alloc(r1, None, n)
+    blocks1 = list(range(300, 300 + 69))
+    meta = conn.build_connector_meta(sched_output([new_req("r1", blocks1, hi)],
+                                                  scheduled={"r1": 1100 - hi}))
+    assert len(meta.loads) == 1
+    ld = meta.loads[0]
+    assert (ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length) == ("s", lo - 24, 24, lo,
+                                                                            hi - lo)
+    # "full" widens the save to [0, hi) once ...
+    assert (meta.saves[0].dst_start, meta.saves[0].length) == (0, 1100)
+    # ... and is downgraded for the next (decode) step
+    cached = SimpleNamespace(req_ids=["r1"], new_block_ids=[None], num_computed_tokens=[1100])
+    meta2 = conn.build_connector_meta(sched_output(cached=cached, scheduled={"r1": 1}))
+    assert (meta2.saves[0].dst_start, meta2.saves[0].length) == (1100, 1)
+
+
+def test_load_is_declined_not_guessed_when_the_store_lost_the_source():
+    conn = scheduler({"store_tokens": 4096})
+    r = request("a", {"session": "x", "load": {"dst_start": 64, "dst_end": 640, "delta": 8}},
+                700)
+    conn.on_new_request(r)
+    assert conn.get_num_new_matched_tokens(r, 64) == (0, False)  # nothing stored yet
+    assert conn._store.misses == 1
+
+
+def test_second_in_flight_writer_on_a_session_is_refused():
+    conn = scheduler()
+    conn.on_new_request(request("a", {"session": "s", "save": True}, 100))
+    conn.on_new_request(request("b", {"session": "s", "save": True}, 100))
+    assert conn._table.session_of("b") is None
+    assert conn._table.conflicts == 1
+    meta = conn.build_connector_meta(sched_output([new_req("b", [1, 2, 3, 4, 5, 6, 7], 0)],
+                                                  scheduled={"b": 100}))
+    assert meta.saves == []  # no session -> pass-through, no save
+
+
+def test_gapfill_accepts_multiple_segments(monkeypatch):
+    monkeypatch.setattr(C, "GAPFILL", True)
+    gapfill.clear()
+    conn = scheduler()
+    conn._store.reserve("s", 0, 2000)
+    loads = [{"dst_start": 100, "dst_end": 600, "delta": 20},
+             {"dst_start": 700, "dst_end": 1500, "delta": -40},
+             {"dst_start": 1600, "dst_end": 1605, "delta": 3}]  # under a block: dropped
+    r = request("g", {"session": "s", "loads": loads, "save": "full"}, 2000)
+    conn.on_new_request(r)
+    n, _ = conn.get_num_new_matched_tokens(r, 0)
+    accepted = conn._multi["g"]
+    assert [(a["dst_start"], a["dst_end"]) for a in accepted] == [(112, 592), (704, 1488)]
+    assert n == (592 - 112) + (1488 - 704)
+    assert "g" in gapfill._offered
+    conn.update_state_after_alloc(r, None, n)
+    meta = conn.build_connector_meta(sched_output([new_req("g", range(200), 0)],
+                                                  scheduled={"g": 2000 - n}))
+    assert [(ld.src_start, ld.delta, ld.length) for ld in meta.loads] == [
+        (92, 20, 480), (744, -40, 784)]
+    conn.request_finished(r, [])
+    assert "g" not in gapfill._offered
+
+
+def test_stats_merges_instances():
+    before = C.stats()["refusals"]
+    conn = scheduler()
+    conn._store.reserve("z", 0, 0)  # empty span: refused
+    assert C.stats()["refusals"] == before + 1
+
+
+# --------------------------------------------------------------- worker (GPU)
+def _oracle_slots(blocks, lo, hi):
+    from oracle import shift_oracle as O
+
+    return O.slots(blocks, lo, hi, BS)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape_kind", ["split", "nhd", "hnd"])
+@pytest.mark.parametrize("batch_save", [False, True])
+def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, batch_save):
+    """Save a prompt layer by layer, then serve an edit turn's load: oracle-exact."""
+    from oracle import shift_oracle as O
+
+    H, D, L, NBLK = 8, 128, 4, 96
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192,
+                                                 "batch_save": batch_save}),
+                                    KVConnectorRole.WORKER, None)
+    g = torch.Generator().manual_seed(7)
+    shapes = {"split": (2, NBLK, BS, H, D), "nhd": (NBLK, BS, H, 2 * D),
+              "hnd": (NBLK, H, BS, 2 * D)}
+    caches = {f"model.layers.{i}.self_attn.attn": torch.randn(shapes[shape_kind], generator=g)
+              .to(torch.bfloat16).to(cuda) for i in range(L)}
+    conn.register_kv_caches(caches)
+    perm = np.random.default_rng(1).permutation(NBLK)
+    blocks0 = perm[:40].tolist()
+
+    # turn 0 saves [0, 600) from blocks0
+    meta = C.ShiftConnectorMetadata(saves=[C._Save("s", 0, 600, blocks0, BS)])
+    conn._store.reserve("s", 0, 600)  # the scheduler's reserve, mirrored
+    conn.bind_connector_metadata(meta)
+    for name, kv in caches.items():
+        conn.save_kv_layer(name, kv, None)
+    conn.wait_for_save()
+    conn.clear_connector_metadata()
+    torch.cuda.synchronize()
+    entry = conn._store._sessions["s"]
+    saved = {n: entry.layers[n][:600].clone() for n in caches}
+    snap = {n: kv.clone() for n, kv in caches.items()}
+
+    # turn 1: [64, 592) moves by +37 into a fresh block table
+    blocks1 = perm[40:80].tolist()
+    meta = C.ShiftConnectorMetadata(loads=[C._Load("s", 64, 37, 101, 528, blocks1, BS)])
+    conn.bind_connector_metadata(meta)
+    conn.start_load_kv(SimpleNamespace(no_compile_layers={}, virtual_engine=0))
+    conn.clear_connector_metadata()
+    torch.cuda.synchronize()
+
+    from marathon_b200.paged import describe
+
+    inv = conn._inv_freq.numpy()
+    tab = O.rope_tables([37], inv)[0]
+    sl1 = _oracle_slots(blocks1, 101, 101 + 528)
+    sl0 = _oracle_slots(blocks0, 0, 600)
+    for name, kv in caches.items():
+        geo = describe(kv, BS, conn._worker.layout)
+        before = O.Paged(snap[name].cpu().view(torch.int16).numpy().view(np.uint16).reshape(-1),
+                         0, geo.v_offset, geo.blk_stride, geo.off_stride, geo.head_stride, BS, H, D)
+        # the save must equal the paged rows it gathered
+        k0, v0 = before.read(sl0)
+        st = saved[name].cpu().view(torch.int16).numpy().view(np.uint16)
+        assert np.array_equal(st[..., :D], k0) and np.array_equal(st[..., D:], v0)
+        # the load must equal the oracle's
+        O.scatter_shifted(st[64:592], before, sl1, tab, O.BF16)
+        got = kv.cpu().view(torch.int16).numpy().view(np.uint16).reshape(-1)
+        assert np.array_equal(got, before.flat), name
+    s = conn._store.stats()
+    assert s["loaded_token_layers"] == 528 * L
+    assert s["saved_token_layers"] == 600 * L

@@ -405,7 +405,7 @@ def test_c3_fp8_full_segment_vs_oracle(cuda):
 
 
 def test_shift_round_trip_property_full_size(cuda):
-    """Load by +delta, save, load by -delta: K returns within 2 bf16 ulp; V bit-exact."""
+    """Load by +delta, save, load by -delta: V bit-exact, K back within bf16 rounding."""
     from marathon_b200.workloads import build, config, scaled
 
     cfg = scaled(config("c2"), layers=4)
@@ -414,7 +414,8 @@ def test_shift_round_trip_property_full_size(cuda):
     view = wl.store_view()
     launcher.load(wl.runs, view, wl.inv_freq, check=True)
     r = wl.runs[0]
-    back = [torch.zeros_like(t) for t in wl.stores[0]]
+    cap = r.paged_start + r.length  # rows land at their new positions
+    back = [torch.zeros((cap, *t.shape[1:]), dtype=t.dtype, device=cuda) for t in wl.stores[0]]
     bview = StoreView(np.array([[t.data_ptr() for t in back]], dtype=np.uint64),
                       np.array([back[0].shape[0]], np.int64), view.st_tok, view.st_head)
     launcher.save([RunSpec(0, r.paged_start, r.length, block_table=wl.block_tables[0],
@@ -431,5 +432,9 @@ def test_shift_round_trip_property_full_size(cuda):
         got = wl.kv[li][bt[pos // BS], pos % BS]
         orig = wl.stores[0][li][r.store_start : r.store_start + r.length]
         assert torch.equal(got[..., D:].view(torch.int16), orig[..., D:].view(torch.int16))
-        dist = O.ulp_distance(bits(got[..., :D]), bits(orig[..., :D]), O.BF16)
-        assert (dist > 2).mean() < 1e-3
+        # two bf16 roundings, each at most 2^-9 of the rotated pair's magnitude, come
+        # back through a rotation: bound the error by the RoPE pair (i, i + D/2)
+        k1, k0 = got[..., :D].float(), orig[..., :D].float()
+        pair = k0[..., : D // 2].abs() + k0[..., D // 2 :].abs()
+        bound = 2.0**-7 * torch.cat((pair, pair), dim=-1)
+        assert bool(((k1 - k0).abs() <= bound).all())
