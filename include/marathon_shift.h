@@ -54,6 +54,7 @@ extern "C" {
 #define MSHIFT_EINVAL 1       /* bad argument (null pointer, size, stride)  */
 #define MSHIFT_EUNSUPPORTED 2 /* dtype / head_size / rotary not compiled    */
 #define MSHIFT_ECUDA 3        /* a CUDA runtime call failed                 */
+#define MSHIFT_ETOOBIG 4      /* exceeds the static scratch of mshift_load_noalloc */
 
 /* ---- device error bits ORed into *err ---------------------------------- */
 #define MSHIFT_EBIT_SLOT 1u    /* slot < 0 or slot >= num_blocks*block_size  */
@@ -170,6 +171,32 @@ MSHIFT_API const char* mshift_strerror(int status);
 
 /* Last CUDA error text seen by the library on this thread (for MSHIFT_ECUDA). */
 MSHIFT_API const char* mshift_last_cuda_error(void);
+
+/*
+ * Allocation-free batched load.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory at load time -- a server
+ * whose whole device pool is handed out at start-up, or a host binding that
+ * can only pass pointers it already owns.  Same work and arguments as
+ * mshift_rope_tables + mshift_load, except that the caller passes the deltas
+ * (device int64[n_deltas]) and inv_freq (device float[rotary/2]) instead of a
+ * table buffer: the tables are built in a fixed 256 KiB array inside the
+ * library's device image (run r's `table` indexes `deltas`).  Limits: at most
+ * mshift_noalloc_max_deltas() (256) deltas and rotary <= 256; beyond that the
+ * call returns MSHIFT_ETOOBIG and launches nothing.  The array is shared by
+ * all calls: calls whose work overlaps on the GPU race on it.  The first call
+ * on a device resolves the array's address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.
+ */
+MSHIFT_API int mshift_load_noalloc(const mshift_paged* paged, int32_t rotary,
+                const mshift_run* runs, int32_t n_runs, int32_t tile_tokens,
+                int32_t tiles_per_layer, int32_t n_layers, void* const* store_ptrs,
+                const int64_t* store_caps, int32_t n_sessions, int64_t st_tok,
+                int64_t st_head, void* const* k_ptrs, void* const* v_ptrs,
+                const int64_t* deltas, int32_t n_deltas, const float* inv_freq,
+                const float* k_scales, uint32_t* err, void* stream);
+
+/* Most distinct deltas one mshift_load_noalloc call accepts. */
+MSHIFT_API int32_t mshift_noalloc_max_deltas(void);
 
 #ifdef __cplusplus
 }

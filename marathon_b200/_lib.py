@@ -17,7 +17,7 @@ import numpy as np
 
 LIB_PATH = Path(__file__).resolve().parent / "libmarathon_shift.so"
 
-OK, EINVAL, EUNSUPPORTED, ECUDA = 0, 1, 2, 3
+OK, EINVAL, EUNSUPPORTED, ECUDA, ETOOBIG = 0, 1, 2, 3, 4
 EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE = 1, 2, 4, 8
 BF16, F16, F32, E4M3 = 0, 1, 2, 3
 
@@ -33,6 +33,8 @@ EXPORTS = (
     "mshift_version",
     "mshift_strerror",
     "mshift_last_cuda_error",
+    "mshift_load_noalloc",
+    "mshift_noalloc_max_deltas",
 )
 
 
@@ -110,6 +112,12 @@ _SIGNATURES = {
     "mshift_version": (ctypes.c_char_p, []),
     "mshift_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "mshift_last_cuda_error": (ctypes.c_char_p, []),
+    "mshift_load_noalloc": (
+        ctypes.c_int,
+        [ctypes.POINTER(Paged), _I32, _P, _I32, _I32, _I32, _I32, _P, _P, _I32, _I64, _I64,
+         _P, _P, _P, _I32, _P, _P, _P, _P],
+    ),
+    "mshift_noalloc_max_deltas": (_I32, []),
 }
 
 _lock = threading.Lock()

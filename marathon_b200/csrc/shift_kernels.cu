@@ -698,10 +698,128 @@ const char* mshift_strerror(int status) {
     case MSHIFT_EINVAL: return "invalid argument";
     case MSHIFT_EUNSUPPORTED: return "unsupported dtype / head_size / rotary combination";
     case MSHIFT_ECUDA: return "CUDA runtime error";
+    case MSHIFT_ETOOBIG:
+      return "request exceeds the static scratch of mshift_load_noalloc (256 deltas, rotary 256)";
     default: return "unknown status";
   }
 }
 
 const char* mshift_last_cuda_error(void) { return g_cuda_error; }
+
+}  // extern "C"
+
+// ============================================ allocation-free batched load
+//
+// For callers that cannot allocate device memory: a process that must not
+// call cudaMalloc once serving has started (a fixed memory budget handed out
+// at start-up, a custom allocator owning the whole pool), or a host whose
+// language binding can only pass pointers it already owns.  The batched load
+// needs one piece of scratch between its two kernels, the rotation tables of
+// the batch's deltas; here they live in a fixed array in the library's own
+// device image, so the caller supplies only inputs and outputs.
+//
+// Limits: at most kNoAllocMaxTables distinct deltas per call and rotary/2 at
+// most kNoAllocMaxHalf (256 x 2 x 128 floats = 256 KiB, held on every GPU that
+// loads the library until the process exits).  Larger requests are rejected
+// with MSHIFT_ETOOBIG before anything is launched.
+//
+// The array is shared by every call in the process: two calls whose work
+// overlaps on the GPU (different streams, no ordering between them) race on
+// it.  Nothing in it has to start at zero: each call's table kernel writes
+// every row the following load kernel reads, in stream order.
+//
+// Set-up: the first call on a device, with that device current, resolves the
+// array's device address with cudaGetSymbolAddress and caches it per device;
+// that first call should come before any stream capture.
+
+namespace mshift {
+constexpr int kNoAllocMaxTables = 256;
+constexpr int kNoAllocMaxHalf = 128;
+}  // namespace mshift
+
+static __device__ __align__(256) float
+    g_noalloc_tables[mshift::kNoAllocMaxTables * 2 * mshift::kNoAllocMaxHalf];
+
+namespace mshift {
+
+struct NoAllocScratch {
+  std::mutex mu;
+  float* tables[kMaxDevices] = {nullptr};
+};
+NoAllocScratch g_noalloc;
+
+// Device address of the scratch tables on the current device (set-up on first use).
+int noalloc_tables(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return MSHIFT_EINVAL;
+  std::lock_guard<std::mutex> lock(g_noalloc.mu);
+  if (g_noalloc.tables[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_tables);
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_noalloc.tables[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc.tables[dev];
+  return MSHIFT_OK;
+}
+
+// The argument checks of the batched load, made before anything is launched.
+int check_load_args(const mshift_paged* paged, int32_t rotary, const mshift_run* runs,
+                    int32_t n_runs, int32_t tile_tokens, int32_t tiles_per_layer,
+                    int32_t n_layers, void* const* store_ptrs, const int64_t* store_caps,
+                    int32_t n_sessions, int64_t st_tok, int64_t st_head, void* const* k_ptrs,
+                    void* const* v_ptrs, const float* k_scales, bool rotating, uint32_t* err) {
+  int st = check_paged(paged);
+  if (st != MSHIFT_OK) return st;
+  if (runs == nullptr || n_runs <= 0 || n_layers <= 0 || tiles_per_layer <= 0) return MSHIFT_EINVAL;
+  if (tile_tokens <= 0 || tile_tokens > kMaxTile) return MSHIFT_EINVAL;
+  if ((int64_t)tiles_per_layer * n_layers > INT32_MAX) return MSHIFT_EINVAL;
+  if (store_ptrs == nullptr || store_caps == nullptr || n_sessions <= 0) return MSHIFT_EINVAL;
+  if (k_ptrs == nullptr || v_ptrs == nullptr || err == nullptr) return MSHIFT_EINVAL;
+  if (st_tok < 0 || st_head < 0) return MSHIFT_EINVAL;
+  const int es = elem_bytes(paged->dtype);
+  if (es == 0) return MSHIFT_EUNSUPPORTED;
+  if (!strides_aligned(es, {paged->blk_stride, paged->off_stride, paged->head_stride, st_tok, st_head}))
+    return MSHIFT_EINVAL;
+  if (find_variant(paged->dtype, paged->head_size, rotary, false) == nullptr)
+    return MSHIFT_EUNSUPPORTED;
+  if (rotating && paged->dtype == MSHIFT_E4M3 && k_scales == nullptr) return MSHIFT_EINVAL;
+  return MSHIFT_OK;
+}
+
+}  // namespace mshift
+
+extern "C" {
+
+int mshift_load_noalloc(const mshift_paged* paged, int32_t rotary, const mshift_run* runs,
+                        int32_t n_runs, int32_t tile_tokens, int32_t tiles_per_layer,
+                        int32_t n_layers, void* const* store_ptrs, const int64_t* store_caps,
+                        int32_t n_sessions, int64_t st_tok, int64_t st_head,
+                        void* const* k_ptrs, void* const* v_ptrs, const int64_t* deltas,
+                        int32_t n_deltas, const float* inv_freq, const float* k_scales,
+                        uint32_t* err, void* stream) {
+  if (n_deltas < 0 || rotary < 0 || (rotary & 1)) return MSHIFT_EINVAL;
+  const int32_t half = rotary / 2;
+  if (n_deltas > kNoAllocMaxTables || half > kNoAllocMaxHalf) return MSHIFT_ETOOBIG;
+  if (n_deltas > 0 && (deltas == nullptr || inv_freq == nullptr)) return MSHIFT_EINVAL;
+  int st = check_load_args(paged, rotary, runs, n_runs, tile_tokens, tiles_per_layer, n_layers,
+                           store_ptrs, store_caps, n_sessions, st_tok, st_head, k_ptrs, v_ptrs,
+                           k_scales, n_deltas > 0, err);
+  if (st != MSHIFT_OK) return st;
+  float* tables = nullptr;
+  st = noalloc_tables(&tables);
+  if (st != MSHIFT_OK) return st;
+  if (n_deltas > 0) {
+    st = mshift_rope_tables(deltas, n_deltas, inv_freq, half, tables, stream);
+    if (st != MSHIFT_OK) return st;
+  }
+  return mshift_load(paged, rotary, runs, n_runs, tile_tokens, tiles_per_layer, n_layers,
+                     store_ptrs, store_caps, n_sessions, st_tok, st_head, k_ptrs, v_ptrs,
+                     n_deltas > 0 ? tables : nullptr, n_deltas, k_scales, err, stream);
+}
+
+int32_t mshift_noalloc_max_deltas(void) { return mshift::kNoAllocMaxTables; }
 
 }  // extern "C"
