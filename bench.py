@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tile-tokens", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=0, help="fewer layers (profiling cases)")
+    ap.add_argument("--no-save", action="store_true", help="skip the save-kernel timing")
     return ap.parse_args()
 
 
@@ -238,7 +240,8 @@ def native_arm(args) -> None:
     from marathon_b200.shift_kernels import Launcher
     from marathon_b200.shift_store import ShiftStore
     from marathon_b200.worker import LoadJob, ShiftWorker
-    from marathon_b200.workloads import build, config
+    from marathon_b200.shift_kernels import RunSpec
+    from marathon_b200.workloads import build, config, scaled
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -249,6 +252,8 @@ def native_arm(args) -> None:
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
 
     cfg = config(args.config)
+    if args.layers:
+        cfg = scaled(cfg, args.layers)
     h_lo, h_hi = head_shard(cfg.heads, rank, world)
     wl = build(cfg, device, head_lo=h_lo, head_hi=h_hi, layout=args.layout)
     fp8 = cfg.dtype == "e4m3"
@@ -311,6 +316,27 @@ def native_arm(args) -> None:
     rank_bytes = wl.algorithmic_bytes()
     ms_per_step = max_ms / args.steps
     value = turn_bytes / (ms_per_step / 1e3) / 1e9
+
+    # the save kernel on the same turn: paged rows of each run back to its store rows
+    save = None
+    if not args.no_save:
+        sruns = [RunSpec(r.session, r.store_start, r.length, block_table=r.block_table,
+                         paged_start=r.paged_start) for r in wl.runs]
+        sp = launcher.prepare_save(sruns, view)
+        launcher.launch(sp)
+        launcher.finish(sp, True)
+        sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(max(10, min(args.steps, 100)))]
+        for a, b in sev:
+            sp = launcher.prepare_save(sruns, view)
+            a.record()
+            launcher.launch(sp)
+            b.record()
+            launcher.finish(sp, False)
+        torch.cuda.synchronize()
+        s_ms = statistics.mean(a.elapsed_time(b) for a, b in sev)
+        save = {"kernel": "move_kernel<save> (mshift_save)", "kernel_ms": round(s_ms, 4),
+                "achieved": round(rank_bytes / (s_ms / 1e3) / 1e9, 1)}
 
     # end to end through the public worker API, from host metadata
     e2e = None
@@ -392,6 +418,7 @@ def native_arm(args) -> None:
                 "traffic": round(traffic) if traffic else None,
             },
             "e2e": e2e,
+            "save": save,
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,

@@ -61,6 +61,7 @@ extern "C" {
 #define MSHIFT_EBIT_STORE 2u   /* store position < 0 or >= session capacity  */
 #define MSHIFT_EBIT_SESSION 4u /* run.session outside [0, n_sessions) or null buffer */
 #define MSHIFT_EBIT_TABLE 8u   /* run.table outside [-1, n_tables)           */
+#define MSHIFT_EBIT_TIMEOUT 16u /* a bulk copy did not complete in time; the launch stopped */
 
 /* ---- element types ----------------------------------------------------- */
 #define MSHIFT_BF16 0

@@ -42,6 +42,24 @@
 
 #include "../../include/marathon_shift.h"
 
+// Tuning knobs (compile-time; the defaults are the measured best on B200):
+//   MSHIFT_MIN_BLOCKS  resident CTAs per SM requested from ptxas (register cap)
+//   MSHIFT_UNITS       (token, head) units each thread keeps in flight
+//   MSHIFT_LOAD_HINT   0: ld.global.cs  1: ld.global.nc  2: ld.global.nc.L1::no_allocate.L2::256B
+//   MSHIFT_STORE_HINT  0: st.global.cs  1: st.global (write-back)
+#ifndef MSHIFT_MIN_BLOCKS
+#define MSHIFT_MIN_BLOCKS 1
+#endif
+#ifndef MSHIFT_UNITS
+#define MSHIFT_UNITS 2
+#endif
+#ifndef MSHIFT_LOAD_HINT
+#define MSHIFT_LOAD_HINT 0
+#endif
+#ifndef MSHIFT_STORE_HINT
+#define MSHIFT_STORE_HINT 0
+#endif
+
 namespace mshift {
 
 constexpr int kThreads = 256;  // threads per CTA
@@ -53,12 +71,27 @@ struct alignas(16) Vec {
 };
 
 __device__ __forceinline__ Vec load_vec(const void* p) {
+#if MSHIFT_LOAD_HINT == 0
   const uint4 r = __ldcs(reinterpret_cast<const uint4*>(p));
   return Vec{{r.x, r.y, r.z, r.w}};
+#elif MSHIFT_LOAD_HINT == 1
+  const uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+  return Vec{{r.x, r.y, r.z, r.w}};
+#else
+  Vec v;
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+      : "l"(p));
+  return v;
+#endif
 }
 
 __device__ __forceinline__ void store_vec(void* p, const Vec& v) {
+#if MSHIFT_STORE_HINT == 0
   __stcs(reinterpret_cast<uint4*>(p), make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]));
+#else
+  *reinterpret_cast<uint4*>(p) = make_uint4(v.w[0], v.w[1], v.w[2], v.w[3]);
+#endif
 }
 
 // ---------------------------------------------------------------- element types
@@ -225,7 +258,7 @@ __device__ __forceinline__ bool aligned16(const void* p) {
 //   SAVE = false: store rows -> paged cache, K rotated (load)
 //   SAVE = true : paged cache -> store rows, bit copy (save)
 template <class E, int D, int ROT, bool SAVE>
-__global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
+__global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const KArgs a) {
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;      // 16-byte vectors per K (or V) row
@@ -332,15 +365,16 @@ __global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
     const bool rotate = !SAVE && HALF > 0 && tab != nullptr && g < NP;
     const int nu = nt * a.heads;
     const int64_t row0 = run.store_start + t0;
-    for (int u = u_first; u < nu; u += 2 * UPP) {
-      // two units per iteration: all eight loads are issued before any store
-      Vec k[2][2], v[2][2];
-      char* sp[2];
-      char* kp[2];
-      char* vp[2];
-      bool live[2];
+    constexpr int U = MSHIFT_UNITS;
+    for (int u = u_first; u < nu; u += U * UPP) {
+      // U units per iteration: all 4*U loads are issued before any store
+      Vec k[U][2], v[U][2];
+      char* sp[U];
+      char* kp[U];
+      char* vp[U];
+      bool live[U];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < U; ++q) {
         const int uu = u + q * UPP;
         live[q] = false;
         if (uu < nu) {
@@ -356,7 +390,7 @@ __global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
         }
       }
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
         if (SAVE) {
           k[q][0] = load_vec(kp[q] + ka * 16);
@@ -371,7 +405,7 @@ __global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
         }
       }
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
         if (rotate) rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC, kscale);
         if (SAVE) {
@@ -386,6 +420,283 @@ __global__ void __launch_bounds__(kThreads) move_kernel(const KArgs a) {
           store_vec(vp[q] + (g + G) * 16, v[q][1]);
         }
       }
+    }
+  }
+}
+
+// ----------------------------------------------------------- TMA bulk load
+//
+// Load direction when every store row is dense ([heads][2*head_size], rows
+// back to back): a tile's store rows are one contiguous range, so they reach
+// shared memory as ONE cp.async.bulk (TMA) per stage, completing on an
+// mbarrier.  One CTA per SM keeps a ring of kBulkStages stages in flight.
+// Warp 0 prepares each stage (run lookup, per-token slot offsets, the run's
+// cos/sin row) and its lane 0 issues the bulk copy; all warps then rotate K
+// from shared memory and write K and V with 128-bit stores.  A caller tile of
+// `tile_tokens` tokens is split into parts that fit one stage.  No
+// multicast, no cluster: each CTA reads only this GPU's memory.
+#ifndef MSHIFT_BULK_STAGES
+#define MSHIFT_BULK_STAGES 3
+#endif
+#ifndef MSHIFT_BULK_STAGE_KB
+#define MSHIFT_BULK_STAGE_KB 64
+#endif
+constexpr int kBulkStages = MSHIFT_BULK_STAGES;
+constexpr int kBulkStageBytes = MSHIFT_BULK_STAGE_KB * 1024;
+constexpr int kBulkMaxPart = 128;          // tokens per stage, upper bound
+constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait rounds before giving up
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: false after kWaitLimit rounds (the caller flags and drains).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void bulk_to_smem(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ Vec lds_vec(const unsigned char* p) {
+  Vec v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+               : "r"(smem_addr(p)));
+  return v;
+}
+
+struct BulkMeta {
+  char* kbase;
+  char* vbase;
+  float kscale;
+  int nt;      // tokens staged (0: nothing to do for this stage)
+  int rotate;  // the stage's table row is valid
+  int pad;
+};
+
+template <class E, int D, int ROT>
+__global__ void __launch_bounds__(kThreads, 1) bulk_load_kernel(const KArgs a, int parts,
+                                                                 int part_tokens) {
+  constexpr int ES = E::kBytes;
+  constexpr int VEC = E::kVec;
+  constexpr int NV = D / VEC;
+  constexpr int HALF = ROT / 2;
+  constexpr int NP = HALF / VEC;
+  constexpr int G = NV / 2;
+  constexpr int UPP = kThreads / G;
+  constexpr int NS = kBulkStages;
+  constexpr int TH = HALF > 0 ? HALF : 4;
+
+  extern __shared__ __align__(128) unsigned char s_data[];
+  __shared__ __align__(8) uint64_t s_full[NS];
+  __shared__ BulkMeta s_meta[NS];
+  __shared__ int64_t s_off[NS][kBulkMaxPart];
+  __shared__ __align__(16) float s_tab[NS][2 * TH];
+  __shared__ int s_abort;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int g = threadIdx.x % G;
+  const int u_first = threadIdx.x / G;
+  const int ka = g < NP ? g : g + NP;
+  const int kb = g < NP ? g + NP : g + G;
+  const int64_t row_bytes = (int64_t)a.heads * 2 * D * ES;
+  const int64_t stage_bytes = (int64_t)part_tokens * row_bytes;
+  const int total = a.tiles_per_layer * a.n_layers * parts;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(&s_full[s], 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+
+  // Warp 0: describe work item `item` in stage `s` and start its bulk copy.
+  auto prepare = [&](int item, int s) {
+    if (item >= total) return;
+    const int w = item / parts;
+    const int part = item - w * parts;
+    const int layer = w / a.tiles_per_layer;
+    const int tile = w - layer * a.tiles_per_layer;
+    int lo = 0, hi = a.n_runs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
+    }
+    const mshift_run run = a.runs[lo];
+    uint32_t bits = 0;
+    const bool sess = run.session >= 0 && run.session < a.n_sessions;
+    const char* store =
+        sess ? static_cast<const char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
+             : nullptr;
+    const int64_t cap = sess ? a.store_caps[run.session] : 0;
+    bool ok = true;
+    if (!sess || store == nullptr || !aligned16(store)) { ok = false; bits |= MSHIFT_EBIT_SESSION; }
+    char* kbase = static_cast<char*>(a.k_ptrs[layer]);
+    char* vbase = static_cast<char*>(a.v_ptrs[layer]);
+    if (kbase == nullptr || vbase == nullptr || !aligned16(kbase) || !aligned16(vbase)) {
+      ok = false;
+      bits |= MSHIFT_EBIT_SLOT;
+    }
+    const float* tab = nullptr;
+    if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
+    else if (run.table != -1) { ok = false; bits |= MSHIFT_EBIT_TABLE; }
+    const int t_tile = (tile - run.tile_begin) * a.tile_tokens;
+    const int t0 = t_tile + part * part_tokens;
+    const int nt = min(min(part_tokens, a.tile_tokens - part * part_tokens), run.len - t0);
+    const int64_t row0 = run.store_start + t0;
+    int nvalid = 0;
+    if (ok && nt > 0 && t_tile >= 0 && row0 >= 0) {
+      const int64_t room = cap - row0;
+      nvalid = room <= 0 ? 0 : (int)(room < nt ? room : nt);
+    }
+    if (ok && nt > 0 && nvalid < nt) bits |= MSHIFT_EBIT_STORE;
+    if (nvalid > 0) {
+      for (int t = lane; t < nt; t += 32) {
+        int64_t slot;
+        bool slot_ok = true;
+        if (run.slots != nullptr) {
+          slot = run.slots[t0 + t];
+        } else {
+          const int64_t pos = run.paged_start + t0 + t;
+          const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
+          slot_ok = bi >= 0 && bi < run.block_table_len;
+          slot = slot_ok ? (int64_t)run.block_table[bi] * a.block_size + pos % a.block_size : -1;
+        }
+        slot_ok = slot_ok && slot >= 0 && slot < a.num_slots;
+        s_off[s][t] = (slot_ok && t < nvalid)
+                          ? (slot / a.block_size) * a.blk_stride + (slot % a.block_size) * a.off_stride
+                          : -1;
+        if (!slot_ok) atomicOr(a.err, MSHIFT_EBIT_SLOT);
+      }
+      if (HALF > 0 && tab != nullptr) {
+        for (int i = lane; i < HALF; i += 32) {
+          s_tab[s][i] = tab[i];
+          s_tab[s][HALF + i] = tab[HALF + i];
+        }
+      }
+    }
+    if (lane == 0) {
+      BulkMeta m;
+      m.kbase = kbase;
+      m.vbase = vbase;
+      m.kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
+      m.nt = nvalid > 0 ? nt : 0;
+      m.rotate = (HALF > 0 && tab != nullptr) ? 1 : 0;
+      m.pad = 0;
+      s_meta[s] = m;
+      if (bits) atomicOr(a.err, bits);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      if (nvalid > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(nvalid * row_bytes);
+        mbar_expect_tx(&s_full[s], bytes);
+        bulk_to_smem(s_data + s * stage_bytes, store + row0 * row_bytes, bytes, &s_full[s]);
+      } else {
+        mbar_arrive(&s_full[s]);
+      }
+    }
+  };
+
+  if (warp == 0)
+    for (int k = 0; k < NS; ++k) prepare(blockIdx.x + k * gridDim.x, k);
+  __syncthreads();
+
+  int k = 0;
+  for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
+    const int s = k % NS;
+    const bool ready = mbar_wait(&s_full[s], (k / NS) & 1);
+    if (!ready) {
+      atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
+      s_abort = 1;
+    }
+    const BulkMeta m = s_meta[s];
+    const unsigned char* stage = s_data + s * stage_bytes;
+    const int nu = ready ? m.nt * a.heads : 0;
+    const bool rotate = m.rotate && g < NP;
+    for (int u = u_first; u < nu; u += 2 * UPP) {
+      Vec kv[2][2], vv[2][2];
+      char* kp[2];
+      char* vp[2];
+      bool live[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int uu = u + q * UPP;
+        live[q] = false;
+        if (uu < nu) {
+          const int t = uu / a.heads;
+          const int h = uu - t * a.heads;
+          const int64_t off = s_off[s][t];
+          if (off >= 0) {
+            live[q] = true;
+            const unsigned char* src = stage + (int64_t)uu * (2 * D * ES);
+            kv[q][0] = lds_vec(src + ka * 16);
+            kv[q][1] = lds_vec(src + kb * 16);
+            vv[q][0] = lds_vec(src + D * ES + g * 16);
+            vv[q][1] = lds_vec(src + D * ES + (g + G) * 16);
+            kp[q] = m.kbase + (off + (int64_t)h * a.head_stride) * ES;
+            vp[q] = m.vbase + (off + (int64_t)h * a.head_stride) * ES;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (!live[q]) continue;
+        if (rotate) rotate_pair<E>(kv[q][0], kv[q][1], s_tab[s] + g * VEC, s_tab[s] + HALF + g * VEC,
+                                   m.kscale);
+        store_vec(kp[q] + ka * 16, kv[q][0]);
+        store_vec(kp[q] + kb * 16, kv[q][1]);
+        store_vec(vp[q] + g * 16, vv[q][0]);
+        store_vec(vp[q] + (g + G) * 16, vv[q][1]);
+      }
+    }
+    __syncthreads();  // every warp is done with stage s: refill it
+    if (s_abort) break;
+    if (warp == 0) prepare(item + NS * gridDim.x, s);
+  }
+  if (s_abort && threadIdx.x == 0) {
+    // a copy never completed: wait (bounded) for every copy this CTA issued
+    // and did not consume, so no bulk copy is left writing shared memory
+    for (int kk = k; kk < k + NS; ++kk) {
+      if (blockIdx.x + kk * gridDim.x < total) (void)mbar_wait(&s_full[kk % NS], (kk / NS) & 1);
     }
   }
 }
@@ -408,15 +719,17 @@ __global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float
 
 // ------------------------------------------------------------------ dispatch
 using KernelFn = void (*)(KArgs);
+using BulkFn = void (*)(KArgs, int, int);
 
 struct Variant {
   int32_t dtype, head_size, rotary;
   KernelFn load;
   KernelFn save;
+  BulkFn bulk;
 };
 
 #define MSHIFT_VARIANT(E, DT, D, R) \
-  {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>}
+  {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>, bulk_load_kernel<E, D, R>}
 
 const Variant kVariants[] = {
     MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 128, 128),
@@ -454,6 +767,8 @@ struct GridCache {
   std::mutex mu;
   int sms[kMaxDevices] = {0};
   int occ[kMaxDevices][2 * kNumVariants] = {{0}};
+  int bulk_smem[kMaxDevices][kNumVariants] = {{0}};  // dynamic smem the bulk kernel is set up for
+  int bulk_occ[kMaxDevices][kNumVariants] = {{0}};
 };
 GridCache g_grid;
 
@@ -518,6 +833,53 @@ int variant_slot(const Variant* v, bool save) {
   return static_cast<int>(v - kVariants) * 2 + (save ? 1 : 0);
 }
 
+#ifndef MSHIFT_LOAD_PATH
+#define MSHIFT_LOAD_PATH 1  // 0: TMA bulk when store rows are dense, 1: always 128-bit loads
+#endif
+
+// Launch the TMA bulk load; returns MSHIFT_EUNSUPPORTED when the geometry does
+// not fit a stage (the caller then uses the 128-bit-load kernel).
+int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStream_t stream) {
+  int part = static_cast<int>(kBulkStageBytes / row_bytes);
+  if (part > args.tile_tokens) part = args.tile_tokens;
+  if (part > kBulkMaxPart) part = kBulkMaxPart;
+  if (part < 1) return MSHIFT_EUNSUPPORTED;
+  const int parts = (args.tile_tokens + part - 1) / part;
+  const int64_t items = (int64_t)args.tiles_per_layer * args.n_layers * parts;
+  if (items > INT32_MAX) return MSHIFT_EUNSUPPORTED;
+  const int smem = static_cast<int>(kBulkStages * part * row_bytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return MSHIFT_EINVAL;
+  const int vi = static_cast<int>(v - kVariants);
+  int grid = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_grid.mu);
+    if (g_grid.sms[dev] == 0) {
+      int sms = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return cuda_fail(e);
+      g_grid.sms[dev] = sms;
+    }
+    if (g_grid.bulk_smem[dev][vi] < smem) {
+      e = cudaFuncSetAttribute(v->bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return cuda_fail(e);
+      int occ = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v->bulk, kThreads, smem);
+      if (e != cudaSuccess) return cuda_fail(e);
+      if (occ < 1) return MSHIFT_EUNSUPPORTED;
+      g_grid.bulk_smem[dev][vi] = smem;
+      g_grid.bulk_occ[dev][vi] = occ;
+    }
+    const int64_t cap = (int64_t)g_grid.sms[dev] * g_grid.bulk_occ[dev][vi];
+    grid = static_cast<int>(items < cap ? items : cap);
+  }
+  v->bulk<<<grid, kThreads, smem, stream>>>(args, parts, part);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
+}
+
 int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_run* runs,
             int32_t n_runs, int32_t tile_tokens, int32_t tiles_per_layer, int32_t n_layers,
             void* const* store_ptrs, const int64_t* store_caps, int32_t n_sessions, int64_t st_tok,
@@ -537,8 +899,8 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
     return MSHIFT_EINVAL;
   const Variant* v = find_variant(paged->dtype, paged->head_size, rotary, save);
   if (v == nullptr) return MSHIFT_EUNSUPPORTED;
-  if (!save) {
-    if (n_tables > 0 && tables == nullptr) return MSHIFT_EINVAL;
+  if (!save && n_tables > 0) {
+    if (tables == nullptr) return MSHIFT_EINVAL;
     if (paged->dtype == MSHIFT_E4M3 && k_scales == nullptr) return MSHIFT_EINVAL;
   }
   KArgs a{};
@@ -564,6 +926,11 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   a.tables = save ? nullptr : tables;
   a.k_scales = save ? nullptr : k_scales;
   a.err = err;
+  const int64_t row_elems = (int64_t)paged->heads * 2 * paged->head_size;
+  if (!save && MSHIFT_LOAD_PATH == 0 && st_head == 2 * paged->head_size && st_tok == row_elems) {
+    const int st = launch_bulk(v, a, row_elems * es, static_cast<cudaStream_t>(stream));
+    if (st != MSHIFT_EUNSUPPORTED) return st;
+  }
   return launch(save ? v->save : v->load, variant_slot(v, save), a,
                 static_cast<cudaStream_t>(stream));
 }
