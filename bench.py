@@ -62,6 +62,7 @@ def parse():
     ap.add_argument("--tile-tokens", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (profiling cases)")
     ap.add_argument("--no-save", action="store_true", help="skip the save-kernel timing")
+    ap.add_argument("--no-alt", action="store_true", help="skip the TMA bulk-load timing")
     return ap.parse_args()
 
 
@@ -317,6 +318,26 @@ def native_arm(args) -> None:
     ms_per_step = max_ms / args.steps
     value = turn_bytes / (ms_per_step / 1e3) / 1e9
 
+    # the alternative load kernel (TMA bulk copies), kernel alone, same turn
+    alt = None
+    if not args.no_alt:
+        from marathon_b200.shift_kernels import set_load_kernel
+
+        prev = set_load_kernel("bulk")
+        try:
+            aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(max(10, min(args.steps, 100)))]
+            step(check=True)
+            for a_, b_ in aev:
+                step(ev=(a_, b_))
+            torch.cuda.synchronize()
+            a_ms = statistics.mean(a_.elapsed_time(b_) for a_, b_ in aev)
+            alt = {"bulk": {"kernel": "bulk_load_kernel (TMA cp.async.bulk, mbarrier ring)",
+                            "kernel_ms": round(a_ms, 4),
+                            "achieved": round(rank_bytes / (a_ms / 1e3) / 1e9, 1)}}
+        finally:
+            set_load_kernel(prev)
+
     # the save kernel on the same turn: paged rows of each run back to its store rows
     save = None
     if not args.no_save:
@@ -416,6 +437,7 @@ def native_arm(args) -> None:
                 "kernel": "move_kernel<load> (mshift_load)", "kernel_ms": round(kernel_ms, 4),
                 "bytes_per_launch": rank_bytes,
                 "traffic": round(traffic) if traffic else None,
+                "alternatives": alt,
             },
             "e2e": e2e,
             "save": save,

@@ -20,6 +20,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libmarathon_shift.so"
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETOOBIG = 0, 1, 2, 3, 4
 EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE = 1, 2, 4, 8
 BF16, F16, F32, E4M3 = 0, 1, 2, 3
+KERNEL_LSU, KERNEL_BULK = 0, 1
 
 #: every symbol the header declares; tests check the library exports them all
 EXPORTS = (
@@ -35,6 +36,7 @@ EXPORTS = (
     "mshift_last_cuda_error",
     "mshift_load_noalloc",
     "mshift_noalloc_max_deltas",
+    "mshift_set_load_kernel",
 )
 
 
@@ -118,6 +120,7 @@ _SIGNATURES = {
          _P, _P, _P, _I32, _P, _P, _P, _P],
     ),
     "mshift_noalloc_max_deltas": (_I32, []),
+    "mshift_set_load_kernel": (ctypes.c_int, [ctypes.c_int]),
 }
 
 _lock = threading.Lock()

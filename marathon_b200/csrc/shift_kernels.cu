@@ -35,6 +35,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -436,10 +437,10 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 // `tile_tokens` tokens is split into parts that fit one stage.  No
 // multicast, no cluster: each CTA reads only this GPU's memory.
 #ifndef MSHIFT_BULK_STAGES
-#define MSHIFT_BULK_STAGES 3
+#define MSHIFT_BULK_STAGES 2
 #endif
 #ifndef MSHIFT_BULK_STAGE_KB
-#define MSHIFT_BULK_STAGE_KB 64
+#define MSHIFT_BULK_STAGE_KB 32
 #endif
 constexpr int kBulkStages = MSHIFT_BULK_STAGES;
 constexpr int kBulkStageBytes = MSHIFT_BULK_STAGE_KB * 1024;
@@ -510,9 +511,12 @@ struct BulkMeta {
   int pad;
 };
 
+constexpr int kBulkConsumerWarps = kThreads / 32;     // warps that rotate and store
+constexpr int kBulkThreads = kThreads + 32;           // + one producer warp
+
 template <class E, int D, int ROT>
-__global__ void __launch_bounds__(kThreads, 1) bulk_load_kernel(const KArgs a, int parts,
-                                                                 int part_tokens) {
+__global__ void __launch_bounds__(kBulkThreads, 1) bulk_load_kernel(const KArgs a, int parts,
+                                                                     int part_tokens) {
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;
@@ -524,133 +528,178 @@ __global__ void __launch_bounds__(kThreads, 1) bulk_load_kernel(const KArgs a, i
   constexpr int TH = HALF > 0 ? HALF : 4;
 
   extern __shared__ __align__(128) unsigned char s_data[];
-  __shared__ __align__(8) uint64_t s_full[NS];
+  __shared__ __align__(8) uint64_t s_full[NS];   // producer -> consumers: stage filled
+  __shared__ __align__(8) uint64_t s_empty[NS];  // consumers -> producer: stage drained
   __shared__ BulkMeta s_meta[NS];
   __shared__ int64_t s_off[NS][kBulkMaxPart];
   __shared__ __align__(16) float s_tab[NS][2 * TH];
-  __shared__ int s_abort;
+  __shared__ volatile int s_abort;
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int g = threadIdx.x % G;
-  const int u_first = threadIdx.x / G;
-  const int ka = g < NP ? g : g + NP;
-  const int kb = g < NP ? g + NP : g + G;
   const int64_t row_bytes = (int64_t)a.heads * 2 * D * ES;
   const int64_t stage_bytes = (int64_t)part_tokens * row_bytes;
   const int total = a.tiles_per_layer * a.n_layers * parts;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(&s_full[s], 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], kBulkConsumerWarps);
+    }
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  __syncthreads();
+  __syncthreads();  // the only CTA-wide barrier: the warps part ways below
 
-  // Warp 0: describe work item `item` in stage `s` and start its bulk copy.
-  auto prepare = [&](int item, int s) {
-    if (item >= total) return;
-    const int w = item / parts;
-    const int part = item - w * parts;
-    const int layer = w / a.tiles_per_layer;
-    const int tile = w - layer * a.tiles_per_layer;
-    int lo = 0, hi = a.n_runs - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
-    }
-    const mshift_run run = a.runs[lo];
-    uint32_t bits = 0;
-    const bool sess = run.session >= 0 && run.session < a.n_sessions;
-    const char* store =
-        sess ? static_cast<const char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
-             : nullptr;
-    const int64_t cap = sess ? a.store_caps[run.session] : 0;
-    bool ok = true;
-    if (!sess || store == nullptr || !aligned16(store)) { ok = false; bits |= MSHIFT_EBIT_SESSION; }
-    char* kbase = static_cast<char*>(a.k_ptrs[layer]);
-    char* vbase = static_cast<char*>(a.v_ptrs[layer]);
-    if (kbase == nullptr || vbase == nullptr || !aligned16(kbase) || !aligned16(vbase)) {
-      ok = false;
-      bits |= MSHIFT_EBIT_SLOT;
-    }
+  if (warp == kBulkConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    // The run and its layer's pointers change only every few items (items
+    // are layer-major), so they are looked up once and kept in registers.
+    int cur_run = -1, cur_layer = -1, next_begin = 0;
+    mshift_run run{};
+    const char* store = nullptr;
+    int64_t cap = 0;
+    char* kbase = nullptr;
+    char* vbase = nullptr;
     const float* tab = nullptr;
-    if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
-    else if (run.table != -1) { ok = false; bits |= MSHIFT_EBIT_TABLE; }
-    const int t_tile = (tile - run.tile_begin) * a.tile_tokens;
-    const int t0 = t_tile + part * part_tokens;
-    const int nt = min(min(part_tokens, a.tile_tokens - part * part_tokens), run.len - t0);
-    const int64_t row0 = run.store_start + t0;
-    int nvalid = 0;
-    if (ok && nt > 0 && t_tile >= 0 && row0 >= 0) {
-      const int64_t room = cap - row0;
-      nvalid = room <= 0 ? 0 : (int)(room < nt ? room : nt);
-    }
-    if (ok && nt > 0 && nvalid < nt) bits |= MSHIFT_EBIT_STORE;
-    if (nvalid > 0) {
-      for (int t = lane; t < nt; t += 32) {
-        int64_t slot;
-        bool slot_ok = true;
-        if (run.slots != nullptr) {
-          slot = run.slots[t0 + t];
-        } else {
-          const int64_t pos = run.paged_start + t0 + t;
-          const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
-          slot_ok = bi >= 0 && bi < run.block_table_len;
-          slot = slot_ok ? (int64_t)run.block_table[bi] * a.block_size + pos % a.block_size : -1;
+    uint32_t desc_bits = 0;
+    bool desc_ok = false;
+    float kscale = 1.0f;
+    int k = 0;
+    for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
+      const int s = k % NS;
+      if (k >= NS) {
+        const bool free_ok = mbar_wait(&s_empty[s], ((k / NS) - 1) & 1);
+        if (!free_ok) {
+          if (lane == 0) atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
+          s_abort = 1;
         }
-        slot_ok = slot_ok && slot >= 0 && slot < a.num_slots;
-        s_off[s][t] = (slot_ok && t < nvalid)
-                          ? (slot / a.block_size) * a.blk_stride + (slot % a.block_size) * a.off_stride
-                          : -1;
-        if (!slot_ok) atomicOr(a.err, MSHIFT_EBIT_SLOT);
+        if (s_abort) break;
       }
-      if (HALF > 0 && tab != nullptr) {
-        for (int i = lane; i < HALF; i += 32) {
-          s_tab[s][i] = tab[i];
-          s_tab[s][HALF + i] = tab[HALF + i];
+      const int w = item / parts;
+      const int part = item - w * parts;
+      const int layer = w / a.tiles_per_layer;
+      const int tile = w - layer * a.tiles_per_layer;
+      const bool same_run = cur_run >= 0 && tile >= run.tile_begin && tile < next_begin;
+      if (!same_run) {
+        int lo = 0, hi = a.n_runs - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
         }
+        cur_run = lo;
+        run = a.runs[lo];
+        next_begin = lo + 1 < a.n_runs ? a.runs[lo + 1].tile_begin : a.tiles_per_layer;
       }
-    }
-    if (lane == 0) {
-      BulkMeta m;
-      m.kbase = kbase;
-      m.vbase = vbase;
-      m.kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
-      m.nt = nvalid > 0 ? nt : 0;
-      m.rotate = (HALF > 0 && tab != nullptr) ? 1 : 0;
-      m.pad = 0;
-      s_meta[s] = m;
-      if (bits) atomicOr(a.err, bits);
-    }
-    __syncwarp();
-    if (lane == 0) {
+      if (!same_run || layer != cur_layer) {
+        cur_layer = layer;
+        desc_bits = 0;
+        desc_ok = true;
+        const bool sess = run.session >= 0 && run.session < a.n_sessions;
+        store = sess ? static_cast<const char*>(
+                           a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
+                     : nullptr;
+        cap = sess ? a.store_caps[run.session] : 0;
+        if (!sess || store == nullptr || !aligned16(store)) {
+          desc_ok = false;
+          desc_bits |= MSHIFT_EBIT_SESSION;
+        }
+        kbase = static_cast<char*>(a.k_ptrs[layer]);
+        vbase = static_cast<char*>(a.v_ptrs[layer]);
+        if (kbase == nullptr || vbase == nullptr || !aligned16(kbase) || !aligned16(vbase)) {
+          desc_ok = false;
+          desc_bits |= MSHIFT_EBIT_SLOT;
+        }
+        tab = nullptr;
+        if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
+        else if (run.table != -1) { desc_ok = false; desc_bits |= MSHIFT_EBIT_TABLE; }
+        kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
+      }
+      uint32_t bits = desc_bits;
+      const bool ok = desc_ok;
+      const int t_tile = (tile - run.tile_begin) * a.tile_tokens;
+      const int t0 = t_tile + part * part_tokens;
+      const int nt = min(min(part_tokens, a.tile_tokens - part * part_tokens), run.len - t0);
+      const int64_t row0 = run.store_start + t0;
+      int nvalid = 0;
+      if (ok && nt > 0 && t_tile >= 0 && row0 >= 0) {
+        const int64_t room = cap - row0;
+        nvalid = room <= 0 ? 0 : (int)(room < nt ? room : nt);
+      }
+      if (ok && nt > 0 && nvalid < nt) bits |= MSHIFT_EBIT_STORE;
       if (nvalid > 0) {
-        const uint32_t bytes = static_cast<uint32_t>(nvalid * row_bytes);
-        mbar_expect_tx(&s_full[s], bytes);
-        bulk_to_smem(s_data + s * stage_bytes, store + row0 * row_bytes, bytes, &s_full[s]);
-      } else {
-        mbar_arrive(&s_full[s]);
+        for (int t = lane; t < nt; t += 32) {
+          int64_t slot;
+          bool slot_ok = true;
+          if (run.slots != nullptr) {
+            slot = run.slots[t0 + t];
+          } else {
+            const int64_t pos = run.paged_start + t0 + t;
+            const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
+            slot_ok = bi >= 0 && bi < run.block_table_len;
+            slot = slot_ok ? (int64_t)run.block_table[bi] * a.block_size + pos % a.block_size : -1;
+          }
+          slot_ok = slot_ok && slot >= 0 && slot < a.num_slots;
+          s_off[s][t] = (slot_ok && t < nvalid) ? (slot / a.block_size) * a.blk_stride +
+                                                      (slot % a.block_size) * a.off_stride
+                                                : -1;
+          if (!slot_ok) atomicOr(a.err, MSHIFT_EBIT_SLOT);
+        }
+        if (HALF > 0 && tab != nullptr) {
+          for (int i = lane; i < HALF; i += 32) {
+            s_tab[s][i] = tab[i];
+            s_tab[s][HALF + i] = tab[HALF + i];
+          }
+        }
+      }
+      if (lane == 0) {
+        BulkMeta m;
+        m.kbase = kbase;
+        m.vbase = vbase;
+        m.kscale = kscale;
+        m.nt = nvalid > 0 ? nt : 0;
+        m.rotate = (HALF > 0 && tab != nullptr) ? 1 : 0;
+        m.pad = 0;
+        s_meta[s] = m;
+        if (bits) atomicOr(a.err, bits);
+      }
+      __syncwarp();  // the lanes' offsets and table are written before lane 0 publishes
+      if (lane == 0) {
+        if (nvalid > 0) {
+          const uint32_t bytes = static_cast<uint32_t>(nvalid * row_bytes);
+          mbar_expect_tx(&s_full[s], bytes);
+          bulk_to_smem(s_data + s * stage_bytes, store + row0 * row_bytes, bytes, &s_full[s]);
+        } else {
+          mbar_arrive(&s_full[s]);
+        }
       }
     }
-  };
+    if (s_abort && lane == 0) {
+      // wait (bounded) for the copies issued into each stage, so none is
+      // left writing shared memory when the CTA exits
+      for (int kk = k - NS < 0 ? 0 : k - NS; kk < k; ++kk)
+        (void)mbar_wait(&s_full[kk % NS], (kk / NS) & 1);
+    }
+    return;
+  }
 
-  if (warp == 0)
-    for (int k = 0; k < NS; ++k) prepare(blockIdx.x + k * gridDim.x, k);
-  __syncthreads();
-
+  // -------------------------------------------------------------- consumers
+  const int g = threadIdx.x % G;
+  const int u_first = threadIdx.x / G;
+  const int ka = g < NP ? g : g + NP;
+  const int kb = g < NP ? g + NP : g + G;
   int k = 0;
   for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
     const int s = k % NS;
-    const bool ready = mbar_wait(&s_full[s], (k / NS) & 1);
-    if (!ready) {
-      atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
+    if (!mbar_wait(&s_full[s], (k / NS) & 1)) {
+      if (lane == 0) atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
       s_abort = 1;
     }
+    if (s_abort) break;
     const BulkMeta m = s_meta[s];
     const unsigned char* stage = s_data + s * stage_bytes;
-    const int nu = ready ? m.nt * a.heads : 0;
+    const int nu = m.nt * a.heads;
     const bool rotate = m.rotate && g < NP;
     for (int u = u_first; u < nu; u += 2 * UPP) {
       Vec kv[2][2], vv[2][2];
@@ -680,24 +729,17 @@ __global__ void __launch_bounds__(kThreads, 1) bulk_load_kernel(const KArgs a, i
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         if (!live[q]) continue;
-        if (rotate) rotate_pair<E>(kv[q][0], kv[q][1], s_tab[s] + g * VEC, s_tab[s] + HALF + g * VEC,
-                                   m.kscale);
+        if (rotate)
+          rotate_pair<E>(kv[q][0], kv[q][1], s_tab[s] + g * VEC, s_tab[s] + HALF + g * VEC,
+                         m.kscale);
         store_vec(kp[q] + ka * 16, kv[q][0]);
         store_vec(kp[q] + kb * 16, kv[q][1]);
         store_vec(vp[q] + g * 16, vv[q][0]);
         store_vec(vp[q] + (g + G) * 16, vv[q][1]);
       }
     }
-    __syncthreads();  // every warp is done with stage s: refill it
-    if (s_abort) break;
-    if (warp == 0) prepare(item + NS * gridDim.x, s);
-  }
-  if (s_abort && threadIdx.x == 0) {
-    // a copy never completed: wait (bounded) for every copy this CTA issued
-    // and did not consume, so no bulk copy is left writing shared memory
-    for (int kk = k; kk < k + NS; ++kk) {
-      if (blockIdx.x + kk * gridDim.x < total) (void)mbar_wait(&s_full[kk % NS], (kk / NS) & 1);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s_empty[s]);  // this warp is done reading stage s
   }
 }
 
@@ -833,9 +875,10 @@ int variant_slot(const Variant* v, bool save) {
   return static_cast<int>(v - kVariants) * 2 + (save ? 1 : 0);
 }
 
-#ifndef MSHIFT_LOAD_PATH
-#define MSHIFT_LOAD_PATH 1  // 0: TMA bulk when store rows are dense, 1: always 128-bit loads
-#endif
+// Which kernel serves loads: MSHIFT_KERNEL_LSU (128-bit loads, the measured
+// fastest on B200) or MSHIFT_KERNEL_BULK (TMA bulk copies through an mbarrier
+// ring; used when the store rows are dense, else the LSU kernel runs).
+std::atomic<int> g_load_kernel{MSHIFT_KERNEL_LSU};
 
 // Launch the TMA bulk load; returns MSHIFT_EUNSUPPORTED when the geometry does
 // not fit a stage (the caller then uses the 128-bit-load kernel).
@@ -866,7 +909,7 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
       e = cudaFuncSetAttribute(v->bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       int occ = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v->bulk, kThreads, smem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v->bulk, kBulkThreads, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       if (occ < 1) return MSHIFT_EUNSUPPORTED;
       g_grid.bulk_smem[dev][vi] = smem;
@@ -875,7 +918,7 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
     const int64_t cap = (int64_t)g_grid.sms[dev] * g_grid.bulk_occ[dev][vi];
     grid = static_cast<int>(items < cap ? items : cap);
   }
-  v->bulk<<<grid, kThreads, smem, stream>>>(args, parts, part);
+  v->bulk<<<grid, kBulkThreads, smem, stream>>>(args, parts, part);
   e = cudaGetLastError();
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
 }
@@ -927,7 +970,8 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   a.k_scales = save ? nullptr : k_scales;
   a.err = err;
   const int64_t row_elems = (int64_t)paged->heads * 2 * paged->head_size;
-  if (!save && MSHIFT_LOAD_PATH == 0 && st_head == 2 * paged->head_size && st_tok == row_elems) {
+  if (!save && g_load_kernel.load(std::memory_order_relaxed) == MSHIFT_KERNEL_BULK &&
+      st_head == 2 * paged->head_size && st_tok == row_elems) {
     const int st = launch_bulk(v, a, row_elems * es, static_cast<cudaStream_t>(stream));
     if (st != MSHIFT_EUNSUPPORTED) return st;
   }
@@ -1055,6 +1099,11 @@ int32_t mshift_default_tile_tokens(int32_t heads) {
 
 int mshift_supported(int32_t dtype, int32_t head_size, int32_t rotary) {
   return find_variant(dtype, head_size, rotary, false) != nullptr ? 1 : 0;
+}
+
+int mshift_set_load_kernel(int kind) {
+  if (kind != MSHIFT_KERNEL_LSU && kind != MSHIFT_KERNEL_BULK) return -1;
+  return g_load_kernel.exchange(kind);
 }
 
 const char* mshift_version(void) { return "marathon_b200 shift 0.1 (sm_100a)"; }

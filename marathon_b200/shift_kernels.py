@@ -37,6 +37,7 @@ __all__ = [
     "rope_shift",
     "rope_tables",
     "scatter_shifted",
+    "set_load_kernel",
     "warmup",
     "inv_freq",
     "RunSpec",
@@ -136,6 +137,19 @@ def rope_shift(delta: int, head_size: int, inv_freq: torch.Tensor, device) -> Ro
     partner[:half] += half
     partner[half:rotary] -= half
     return RopeShift(int(delta), cos, sgn, partner, torch.cat((c, c)), torch.cat((s, s)), table)
+
+
+def set_load_kernel(kind: str) -> str:
+    """Select the load kernel process-wide: ``"lsu"`` (default) or ``"bulk"`` (TMA).
+
+    Returns the previous selection.  Both write identical bits; they differ in
+    how the store rows reach the SM (128-bit loads vs one bulk copy per tile).
+    """
+    codes = {"lsu": _lib.KERNEL_LSU, "bulk": _lib.KERNEL_BULK}
+    if kind not in codes:
+        raise ShiftError(f"unknown load kernel {kind!r}")
+    prev = _lib.load().mshift_set_load_kernel(codes[kind])
+    return {v: k for k, v in codes.items()}[prev]
 
 
 # ------------------------------------------------------------ error words

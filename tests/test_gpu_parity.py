@@ -57,6 +57,14 @@ def inv128():
     return sk.inv_freq(128, 1e6)
 
 
+@pytest.fixture(params=["lsu", "bulk"])
+def load_kernel(request, cuda):
+    """Run a batched-load test through each load kernel (128-bit loads / TMA bulk)."""
+    prev = sk.set_load_kernel(request.param)
+    yield request.param
+    sk.set_load_kernel(prev)
+
+
 # ------------------------------------------------------------------ tables
 def test_rope_tables_bit_identical_to_oracle(cuda, golden):
     deltas = golden["table_deltas"]
@@ -232,22 +240,22 @@ def _run_batched_load(cuda, layout, dtype=O.BF16, heads=H, d=D, rotary=None, see
 
 
 @pytest.mark.parametrize("layout", ["nhd", "hnd", "split", "split_blocks"])
-def test_batched_load_all_layouts_bit_exact(cuda, layout):
+def test_batched_load_all_layouts_bit_exact(cuda, load_kernel, layout):
     _run_batched_load(cuda, layout)
 
 
 @pytest.mark.parametrize("dtype", [O.F16, O.E4M3, O.F32])
-def test_batched_load_dtypes_bit_exact(cuda, dtype):
+def test_batched_load_dtypes_bit_exact(cuda, load_kernel, dtype):
     _run_batched_load(cuda, "nhd", dtype=dtype, seed=5)
 
 
 @pytest.mark.parametrize("d,rotary", [(256, 64), (128, 64), (64, 64), (256, 256)])
-def test_batched_load_head_geometries(cuda, d, rotary):
+def test_batched_load_head_geometries(cuda, load_kernel, d, rotary):
     _run_batched_load(cuda, "nhd", d=d, rotary=rotary, seed=d + rotary)
 
 
 @pytest.mark.parametrize("heads", [1, 2, 4])
-def test_batched_load_head_shards(cuda, heads):
+def test_batched_load_head_shards(cuda, load_kernel, heads):
     """The per-rank shapes of head-sharded tensor parallelism (8 heads over 8/4/2 ranks)."""
     _run_batched_load(cuda, "nhd", heads=heads, seed=heads)
 
@@ -287,7 +295,7 @@ def test_batched_save_bit_exact_and_round_trip(cuda, layout):
     assert torch.equal(one, fresh[0][1])
 
 
-def test_rejected_tokens_raise_without_fault_and_good_tokens_land(cuda):
+def test_rejected_tokens_raise_without_fault_and_good_tokens_land(cuda, load_kernel):
     """Bad descriptors are flagged by the kernel (error word), never dereferenced."""
     g = torch.Generator().manual_seed(3)
     store = rand((64, H, 2 * D), O.BF16, g).to(cuda)
@@ -337,7 +345,7 @@ def _torch_reference_rows(store_rows: torch.Tensor, table: torch.Tensor) -> torc
 
 
 @pytest.mark.parametrize("name", ["c0", "c1", "c2"])
-def test_baseline_configs_full_size_vs_torch_fp32(cuda, name):
+def test_baseline_configs_full_size_vs_torch_fp32(cuda, load_kernel, name):
     """Every layer of configs c0-c2 at full size, against torch fp32 on the same GPU."""
     from marathon_b200.workloads import build, config
 
@@ -383,7 +391,7 @@ def test_c2_two_layers_vs_numpy_oracle(cuda):
         assert np.array_equal(g[..., D:], rows[..., D:])
 
 
-def test_c3_fp8_full_segment_vs_oracle(cuda):
+def test_c3_fp8_full_segment_vs_oracle(cuda, load_kernel):
     """c3 (e4m3, per-layer scales): 2 layers of the full segment through the oracle."""
     from marathon_b200.workloads import build, config, scaled
 
