@@ -430,12 +430,13 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 // Load direction when every store row is dense ([heads][2*head_size], rows
 // back to back): a tile's store rows are one contiguous range, so they reach
 // shared memory as ONE cp.async.bulk (TMA) per stage, completing on an
-// mbarrier.  One CTA per SM keeps a ring of kBulkStages stages in flight.
-// Warp 0 prepares each stage (run lookup, per-token slot offsets, the run's
-// cos/sin row) and its lane 0 issues the bulk copy; all warps then rotate K
-// from shared memory and write K and V with 128-bit stores.  A caller tile of
-// `tile_tokens` tokens is split into parts that fit one stage.  No
-// multicast, no cluster: each CTA reads only this GPU's memory.
+// mbarrier.  Each CTA keeps a ring of kBulkStages stages in flight.  A
+// producer warp prepares each stage (run lookup, per-token slot offsets, the
+// run's cos/sin row) and its lane 0 issues the bulk copy; eight consumer
+// warps rotate K from shared memory and write K and V with 128-bit stores,
+// then release the stage through its "empty" mbarrier.  A caller tile of
+// `tile_tokens` tokens is split into parts that fit one stage.  Every copy is
+// a plain per-CTA copy from this GPU's own memory.
 #ifndef MSHIFT_BULK_STAGES
 #define MSHIFT_BULK_STAGES 2
 #endif
