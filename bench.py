@@ -287,9 +287,11 @@ def native_arm(args) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    while time.perf_counter() - t_warm < 0.3:  # let the sampler see the load
-        step()
-    torch.cuda.synchronize()
+    # keep the GPU busy until nvidia-smi (slow to start) has sampled under load
+    while time.perf_counter() - t_warm < 1.5:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
 
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
@@ -323,7 +325,7 @@ def native_arm(args) -> None:
     if not args.no_alt:
         from marathon_b200.shift_kernels import set_load_kernel
 
-        prev = set_load_kernel("bulk")
+        prev = set_load_kernel("lsu" if fp8 else "bulk")  # the one auto did not pick
         try:
             aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(max(10, min(args.steps, 100)))]
@@ -332,9 +334,10 @@ def native_arm(args) -> None:
                 step(ev=(a_, b_))
             torch.cuda.synchronize()
             a_ms = statistics.mean(a_.elapsed_time(b_) for a_, b_ in aev)
-            alt = {"bulk": {"kernel": "bulk_load_kernel (TMA cp.async.bulk, mbarrier ring)",
-                            "kernel_ms": round(a_ms, 4),
-                            "achieved": round(rank_bytes / (a_ms / 1e3) / 1e9, 1)}}
+            name = ("lsu", "move_kernel<load> (128-bit loads)") if fp8 else (
+                "bulk", "bulk_load_kernel (TMA cp.async.bulk, mbarrier ring)")
+            alt = {name[0]: {"kernel": name[1], "kernel_ms": round(a_ms, 4),
+                             "achieved": round(rank_bytes / (a_ms / 1e3) / 1e9, 1)}}
         finally:
             set_load_kernel(prev)
 
@@ -396,8 +399,10 @@ def native_arm(args) -> None:
 
     peak, peak_kind = peaks()
     achieved = rank_bytes / (kernel_ms / 1e3) / 1e9
-    units = cfg.shifted_tokens * cfg.layers
+    units = cfg.shifted_tokens * cfg.layers  # (token, layer) units of the whole turn
     traffic = traffic_for(cfg.name, args.layout, units)
+    if traffic is not None:
+        traffic *= (h_hi - h_lo) / cfg.heads  # this rank's head shard of each unit
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         s = CpuPath(cfg).sample(args.cpu_seconds)
@@ -434,7 +439,9 @@ def native_arm(args) -> None:
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_8tbs": round(achieved / 8000.0, 4),
-                "kernel": "move_kernel<load> (mshift_load)", "kernel_ms": round(kernel_ms, 4),
+                "kernel": ("bulk_load_kernel (mshift_load, TMA)" if fp8
+                           else "move_kernel<load> (mshift_load)"),
+                "kernel_ms": round(kernel_ms, 4),
                 "bytes_per_launch": rank_bytes,
                 "traffic": round(traffic) if traffic else None,
                 "alternatives": alt,

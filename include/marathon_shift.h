@@ -164,15 +164,18 @@ MSHIFT_API int32_t mshift_plan_tiles(mshift_run* runs, int32_t n_runs, int32_t t
 MSHIFT_API int32_t mshift_default_tile_tokens(int32_t heads);
 
 /*
- * Load kernel selection, process-wide.  MSHIFT_KERNEL_LSU (default): every
- * byte through 128-bit loads/stores.  MSHIFT_KERNEL_BULK: each tile's store
- * rows reach shared memory in one TMA bulk copy (cp.async.bulk, mbarrier
- * ring, producer warp) when the store rows are dense; otherwise the LSU
- * kernel runs.  Returns the previous kind, or -1 for an unknown kind.  No
- * counterpart in the reference (its one Triton kernel had no alternative).
+ * Load kernel selection, process-wide.  MSHIFT_KERNEL_LSU: every byte through
+ * 128-bit loads/stores.  MSHIFT_KERNEL_BULK: each tile's store rows reach
+ * shared memory in one TMA bulk copy (cp.async.bulk, mbarrier ring, producer
+ * warp) when the store rows are dense; otherwise the LSU kernel runs.
+ * MSHIFT_KERNEL_AUTO (default): BULK for e4m3 caches, LSU for the others (the
+ * faster of the two for each on B200).  Returns the previous kind, or -1 for
+ * an unknown kind.  No counterpart in the reference (its one Triton kernel had
+ * no alternative).
  */
 #define MSHIFT_KERNEL_LSU 0
 #define MSHIFT_KERNEL_BULK 1
+#define MSHIFT_KERNEL_AUTO 2
 MSHIFT_API int mshift_set_load_kernel(int kind);
 
 /* 1 if (dtype, head_size, rotary) has a compiled kernel, else 0. */

@@ -20,7 +20,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libmarathon_shift.so"
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETOOBIG = 0, 1, 2, 3, 4
 EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE = 1, 2, 4, 8
 BF16, F16, F32, E4M3 = 0, 1, 2, 3
-KERNEL_LSU, KERNEL_BULK = 0, 1
+KERNEL_LSU, KERNEL_BULK, KERNEL_AUTO = 0, 1, 2
 
 #: every symbol the header declares; tests check the library exports them all
 EXPORTS = (

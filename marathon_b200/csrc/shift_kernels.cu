@@ -96,130 +96,156 @@ __device__ __forceinline__ void store_vec(void* p, const Vec& v) {
 }
 
 // ---------------------------------------------------------------- element types
+// Each type converts one 32-bit word of a 16-byte vector (kPer elements) to
+// fp32 and back, rounding to nearest even.
 struct Bf16 {
-  static constexpr int kBytes = 2, kVec = 8;
+  static constexpr int kBytes = 2, kVec = 8, kPer = 2;
   static constexpr bool kScaled = false;
-  __device__ static void unpack(const Vec& v, float* f) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[2 * i] = __uint_as_float(v.w[i] << 16);
-      f[2 * i + 1] = __uint_as_float(v.w[i] & 0xffff0000u);
-    }
+  __device__ static void unpack(uint32_t w, float* f) {
+    f[0] = __uint_as_float(w << 16);
+    f[1] = __uint_as_float(w & 0xffff0000u);
   }
-  __device__ static Vec pack(const float* f) {
-    Vec v;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-      v.w[i] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    return v;
+  __device__ static uint32_t pack(const float* f) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f[0], f[1]);
+    return *reinterpret_cast<const uint32_t*>(&h);
   }
 };
 
 struct F16 {
-  static constexpr int kBytes = 2, kVec = 8;
+  static constexpr int kBytes = 2, kVec = 8, kPer = 2;
   static constexpr bool kScaled = false;
-  __device__ static void unpack(const Vec& v, float* f) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half2 h = *reinterpret_cast<const __half2*>(&v.w[i]);
-      const float2 p = __half22float2(h);
-      f[2 * i] = p.x;
-      f[2 * i + 1] = p.y;
-    }
+  __device__ static void unpack(uint32_t w, float* f) {
+    const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    f[0] = p.x;
+    f[1] = p.y;
   }
-  __device__ static Vec pack(const float* f) {
-    Vec v;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-      v.w[i] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    return v;
+  __device__ static uint32_t pack(const float* f) {
+    const __half2 h = __floats2half2_rn(f[0], f[1]);
+    return *reinterpret_cast<const uint32_t*>(&h);
   }
 };
 
 struct F32 {
-  static constexpr int kBytes = 4, kVec = 4;
+  static constexpr int kBytes = 4, kVec = 4, kPer = 1;
   static constexpr bool kScaled = false;
-  __device__ static void unpack(const Vec& v, float* f) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(v.w[i]);
-  }
-  __device__ static Vec pack(const float* f) {
-    Vec v;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v.w[i] = __float_as_uint(f[i]);
-    return v;
-  }
+  __device__ static void unpack(uint32_t w, float* f) { f[0] = __uint_as_float(w); }
+  __device__ static uint32_t pack(const float* f) { return __float_as_uint(f[0]); }
 };
 
 struct E4m3 {
-  static constexpr int kBytes = 1, kVec = 16;
+  static constexpr int kBytes = 1, kVec = 16, kPer = 4;
   static constexpr bool kScaled = true;
-  __device__ static void unpack(const Vec& v, float* f) {
+  __device__ static void unpack(uint32_t w, float* f) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const __nv_fp8x2_storage_t pair =
-            static_cast<__nv_fp8x2_storage_t>((v.w[i] >> (16 * j)) & 0xffffu);
-        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-        f[4 * i + 2 * j] = p.x;
-        f[4 * i + 2 * j + 1] = p.y;
-      }
+    for (int j = 0; j < 2; ++j) {
+      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>((w >> (16 * j)) & 0xffffu);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+      const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+      f[2 * j] = p.x;
+      f[2 * j + 1] = p.y;
     }
   }
-  __device__ static Vec pack(const float* f) {
-    Vec v;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i], f[4 * i + 1]),
-                                                   __NV_SATFINITE, __NV_E4M3);
-      const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f[4 * i + 2], f[4 * i + 3]),
-                                                   __NV_SATFINITE, __NV_E4M3);
-      v.w[i] = (lo & 0xffffu) | ((hi & 0xffffu) << 16);
-    }
-    return v;
+  __device__ static uint32_t pack(const float* f) {
+    const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(f[0], f[1]), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(f[2], f[3]), __NV_SATFINITE, __NV_E4M3);
+    return (lo & 0xffffu) | ((hi & 0xffffu) << 16);
   }
 };
 
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b);
+
+// e4m3 codes of (r.x / s, r.y / s), each exactly the saturating
+// round-to-nearest-even of the correctly rounded quotient __fdiv_rn(r, s).
+// q = r * (1/s) is within 2.5 ulp of that quotient.  Converting q*(1-2^-21)
+// and q*(1+2^-21) (an interval of at least 4 ulp on each side of q) gives the
+// same code for both ends exactly when every value in between, the quotient
+// included, rounds to that code (the conversion is monotonic); only when the
+// ends differ -- q sits next to an e4m3 rounding boundary -- is the quotient
+// formed by division.
+__device__ __forceinline__ uint32_t requant2(float2 r, float s, float inv) {
+  const float2 q = mul2_rn(r, make_float2(inv, inv));
+  const float2 lo = mul2_rn(q, make_float2(0.99999952316284180f, 0.99999952316284180f));
+  const float2 hi = mul2_rn(q, make_float2(1.00000047683715820f, 1.00000047683715820f));
+  const uint32_t c_lo = __nv_cvt_float2_to_fp8x2(lo, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
+  const uint32_t c_hi = __nv_cvt_float2_to_fp8x2(hi, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
+  if (c_lo == c_hi) return c_lo;
+  const float2 exact = make_float2(__fdiv_rn(r.x, s), __fdiv_rn(r.y, s));
+  return __nv_cvt_float2_to_fp8x2(exact, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
+}
+
+// Packed fp32x2 multiply, each lane rounded to nearest.  Measured on B200
+// (sm_100a, CUDA 12.9): a packed multiply feeding a packed add was fused into
+// an FMA even with explicit .rn modifiers, so the adds that follow stay scalar
+// (__fadd_rn / __fsub_rn are never merged with a multiply).
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
 // Rotate one pair of partner vectors in place: `a` holds elements
 // [i0, i0+VEC) of the first rotary half, `b` the same elements of the second.
+// Works one 32-bit word (kPer elements) at a time to keep few values live; the
+// products of two elements share one packed fp32x2 multiply (each lane rounds
+// on its own), the sums are scalar, so the results are those of the scalar
+// __fmul_rn / __fsub_rn / __fadd_rn sequence.
 template <class E>
 __device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, const float* sn,
-                                            float scale) {
-  constexpr int V = E::kVec;
-  float x[V], y[V], c[V], s[V];
-  E::unpack(a, x);
-  E::unpack(b, y);
+                                            float scale, float inv_scale) {
+  constexpr int P = E::kPer;
 #pragma unroll
-  for (int e = 0; e < V; e += 4) {
-    const float4 c4 = *reinterpret_cast<const float4*>(cs + e);
-    const float4 s4 = *reinterpret_cast<const float4*>(sn + e);
-    c[e] = c4.x, c[e + 1] = c4.y, c[e + 2] = c4.z, c[e + 3] = c4.w;
-    s[e] = s4.x, s[e + 1] = s4.y, s[e + 2] = s4.z, s[e + 3] = s4.w;
-  }
+  for (int w = 0; w < 4; ++w) {
+    float x[P], y[P];
+    uint32_t qa = 0, qb = 0;  // requantised codes (scaled types)
+    E::unpack(a.w[w], x);
+    E::unpack(b.w[w], y);
+    if constexpr (P == 1) {
+      const float c = cs[w], s = sn[w];
+      float xe = x[0], ye = y[0];
+      if constexpr (E::kScaled) {
+        xe = __fmul_rn(xe, scale);
+        ye = __fmul_rn(ye, scale);
+      }
+      x[0] = __fsub_rn(__fmul_rn(xe, c), __fmul_rn(ye, s));
+      y[0] = __fadd_rn(__fmul_rn(ye, c), __fmul_rn(xe, s));
+    } else {
 #pragma unroll
-  for (int e = 0; e < V; ++e) {
-    float xe = x[e], ye = y[e];
-    if constexpr (E::kScaled) {
-      xe = __fmul_rn(xe, scale);
-      ye = __fmul_rn(ye, scale);
+      for (int j = 0; j < P / 2; ++j) {
+        const float2 c = *reinterpret_cast<const float2*>(cs + P * w + 2 * j);
+        const float2 s = *reinterpret_cast<const float2*>(sn + P * w + 2 * j);
+        float2 x2 = make_float2(x[2 * j], x[2 * j + 1]);
+        float2 y2 = make_float2(y[2 * j], y[2 * j + 1]);
+        if constexpr (E::kScaled) {
+          const float2 sc = make_float2(scale, scale);
+          x2 = mul2_rn(x2, sc);
+          y2 = mul2_rn(y2, sc);
+        }
+        // packed products, scalar adds: __fadd_rn / __fsub_rn are never merged
+        // with a multiply, so every product is rounded before it is added
+        const float2 xc = mul2_rn(x2, c), ys = mul2_rn(y2, s);
+        const float2 yc = mul2_rn(y2, c), xs = mul2_rn(x2, s);
+        const float2 ra = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+        const float2 rb = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+        if constexpr (E::kScaled) {
+          qa |= requant2(ra, scale, inv_scale) << (16 * j);
+          qb |= requant2(rb, scale, inv_scale) << (16 * j);
+        } else {
+          x[2 * j] = ra.x, x[2 * j + 1] = ra.y;
+          y[2 * j] = rb.x, y[2 * j + 1] = rb.y;
+        }
+      }
     }
-    float ra = __fsub_rn(__fmul_rn(xe, c[e]), __fmul_rn(ye, s[e]));
-    float rb = __fadd_rn(__fmul_rn(ye, c[e]), __fmul_rn(xe, s[e]));
     if constexpr (E::kScaled) {
-      ra = __fdiv_rn(ra, scale);
-      rb = __fdiv_rn(rb, scale);
+      a.w[w] = qa;
+      b.w[w] = qb;
+    } else {
+      a.w[w] = E::pack(x);
+      b.w[w] = E::pack(y);
     }
-    x[e] = ra;
-    y[e] = rb;
   }
-  a = E::pack(x);
-  b = E::pack(y);
 }
 
 // ------------------------------------------------------------------ arguments
@@ -329,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
     const int nt = min(a.tile_tokens, run.len - t0);
     const bool tile_ok = ok_desc && nt > 0 && t0 >= 0;
     const float kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
+    const float kinv = E::kScaled ? __frcp_rn(kscale) : 1.0f;
 
     __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn
     if (threadIdx.x == 0 && bits) atomicOr(a.err, bits);
@@ -408,7 +435,8 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 #pragma unroll
       for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
-        if (rotate) rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC, kscale);
+        if (rotate)
+          rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC, kscale, kinv);
         if (SAVE) {
           store_vec(sp[q] + ka * 16, k[q][0]);
           store_vec(sp[q] + kb * 16, k[q][1]);
@@ -430,21 +458,41 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 // Load direction when every store row is dense ([heads][2*head_size], rows
 // back to back): a tile's store rows are one contiguous range, so they reach
 // shared memory as ONE cp.async.bulk (TMA) per stage, completing on an
-// mbarrier.  Each CTA keeps a ring of kBulkStages stages in flight.  A
+// mbarrier.  Each CTA keeps a ring of bulk_stages<E>() stages in flight.  A
 // producer warp prepares each stage (run lookup, per-token slot offsets, the
 // run's cos/sin row) and its lane 0 issues the bulk copy; eight consumer
 // warps rotate K from shared memory and write K and V with 128-bit stores,
 // then release the stage through its "empty" mbarrier.  A caller tile of
 // `tile_tokens` tokens is split into parts that fit one stage.  Every copy is
 // a plain per-CTA copy from this GPU's own memory.
-#ifndef MSHIFT_BULK_STAGES
-#define MSHIFT_BULK_STAGES 2
+// Stage ring per element type (measured best on B200, c2/c3 turns): three
+// stages of 32 KiB for e4m3, whose consumers are busier with arithmetic, and
+// of 24 KiB for 16/32-bit types; two CTAs per SM either way.
+// MSHIFT_BULK_STAGES / MSHIFT_BULK_STAGE_KB override both (tuning sweeps).
+template <class E>
+struct BulkCfg {
+  static constexpr int kStages = 3;
+  static constexpr int kStageBytes = (E::kScaled ? 32 : 24) * 1024;
+};
+#ifdef MSHIFT_BULK_STAGES
+constexpr int kBulkStagesOverride = MSHIFT_BULK_STAGES;
+#else
+constexpr int kBulkStagesOverride = 0;
 #endif
-#ifndef MSHIFT_BULK_STAGE_KB
-#define MSHIFT_BULK_STAGE_KB 32
+#ifdef MSHIFT_BULK_STAGE_KB
+constexpr int kBulkStageBytesOverride = MSHIFT_BULK_STAGE_KB * 1024;
+#else
+constexpr int kBulkStageBytesOverride = 0;
 #endif
-constexpr int kBulkStages = MSHIFT_BULK_STAGES;
-constexpr int kBulkStageBytes = MSHIFT_BULK_STAGE_KB * 1024;
+template <class E>
+__host__ __device__ constexpr int bulk_stages() {
+  return kBulkStagesOverride ? kBulkStagesOverride : BulkCfg<E>::kStages;
+}
+template <class E>
+__host__ __device__ constexpr int bulk_stage_bytes() {
+  return kBulkStageBytesOverride ? kBulkStageBytesOverride : BulkCfg<E>::kStageBytes;
+}
+constexpr int kBulkMaxStages = 8;
 constexpr int kBulkMaxPart = 128;          // tokens per stage, upper bound
 constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait rounds before giving up
 
@@ -507,16 +555,24 @@ struct BulkMeta {
   char* kbase;
   char* vbase;
   float kscale;
+  float kinv;  // 1 / kscale rounded (e4m3 requantisation)
   int nt;      // tokens staged (0: nothing to do for this stage)
   int rotate;  // the stage's table row is valid
-  int pad;
 };
 
-constexpr int kBulkConsumerWarps = kThreads / 32;     // warps that rotate and store
-constexpr int kBulkThreads = kThreads + 32;           // + one producer warp
+#ifndef MSHIFT_BULK_CONSUMER_WARPS
+#define MSHIFT_BULK_CONSUMER_WARPS 8
+#endif
+#ifndef MSHIFT_BULK_MIN_BLOCKS
+#define MSHIFT_BULK_MIN_BLOCKS 2
+#endif
+constexpr int kBulkConsumerWarps = MSHIFT_BULK_CONSUMER_WARPS;  // warps that rotate and store
+constexpr int kBulkConsumers = kBulkConsumerWarps * 32;
+constexpr int kBulkThreads = kBulkConsumers + 32;              // + one producer warp
 
 template <class E, int D, int ROT>
-__global__ void __launch_bounds__(kBulkThreads, 1) bulk_load_kernel(const KArgs a, int parts,
+__global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_load_kernel(
+    const KArgs a, int parts,
                                                                      int part_tokens) {
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
@@ -524,8 +580,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_load_kernel(const KArgs 
   constexpr int HALF = ROT / 2;
   constexpr int NP = HALF / VEC;
   constexpr int G = NV / 2;
-  constexpr int UPP = kThreads / G;
-  constexpr int NS = kBulkStages;
+  constexpr int UPP = kBulkConsumers / G;
+  constexpr int NS = bulk_stages<E>();
+  static_assert(NS >= 2 && NS <= kBulkMaxStages, "stage ring of 2..8");
   constexpr int TH = HALF > 0 ? HALF : 4;
 
   extern __shared__ __align__(128) unsigned char s_data[];
@@ -659,9 +716,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_load_kernel(const KArgs 
         m.kbase = kbase;
         m.vbase = vbase;
         m.kscale = kscale;
+        m.kinv = E::kScaled ? __frcp_rn(kscale) : 1.0f;
         m.nt = nvalid > 0 ? nt : 0;
         m.rotate = (HALF > 0 && tab != nullptr) ? 1 : 0;
-        m.pad = 0;
         s_meta[s] = m;
         if (bits) atomicOr(a.err, bits);
       }
@@ -732,7 +789,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_load_kernel(const KArgs 
         if (!live[q]) continue;
         if (rotate)
           rotate_pair<E>(kv[q][0], kv[q][1], s_tab[s] + g * VEC, s_tab[s] + HALF + g * VEC,
-                         m.kscale);
+                         m.kscale, m.kinv);
         store_vec(kp[q] + ka * 16, kv[q][0]);
         store_vec(kp[q] + kb * 16, kv[q][1]);
         store_vec(vp[q] + g * 16, vv[q][0]);
@@ -769,10 +826,12 @@ struct Variant {
   KernelFn load;
   KernelFn save;
   BulkFn bulk;
+  int bulk_stages, bulk_stage_bytes;
 };
 
-#define MSHIFT_VARIANT(E, DT, D, R) \
-  {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>, bulk_load_kernel<E, D, R>}
+#define MSHIFT_VARIANT(E, DT, D, R)                                                    \
+  {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>,                 \
+   bulk_load_kernel<E, D, R>, bulk_stages<E>(), bulk_stage_bytes<E>()}
 
 const Variant kVariants[] = {
     MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 128, 128),
@@ -876,22 +935,24 @@ int variant_slot(const Variant* v, bool save) {
   return static_cast<int>(v - kVariants) * 2 + (save ? 1 : 0);
 }
 
-// Which kernel serves loads: MSHIFT_KERNEL_LSU (128-bit loads, the measured
-// fastest on B200) or MSHIFT_KERNEL_BULK (TMA bulk copies through an mbarrier
-// ring; used when the store rows are dense, else the LSU kernel runs).
-std::atomic<int> g_load_kernel{MSHIFT_KERNEL_LSU};
+// Which kernel serves loads: MSHIFT_KERNEL_LSU (128-bit loads), MSHIFT_KERNEL_BULK
+// (TMA bulk copies through an mbarrier ring; used when the store rows are
+// dense, else the LSU kernel runs) or MSHIFT_KERNEL_AUTO (the measured faster
+// one on B200: TMA for e4m3, whose consumer warps are busy with the
+// dequantise/requantise arithmetic, 128-bit loads for 16/32-bit types).
+std::atomic<int> g_load_kernel{MSHIFT_KERNEL_AUTO};
 
 // Launch the TMA bulk load; returns MSHIFT_EUNSUPPORTED when the geometry does
 // not fit a stage (the caller then uses the 128-bit-load kernel).
 int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStream_t stream) {
-  int part = static_cast<int>(kBulkStageBytes / row_bytes);
+  int part = static_cast<int>(v->bulk_stage_bytes / row_bytes);
   if (part > args.tile_tokens) part = args.tile_tokens;
   if (part > kBulkMaxPart) part = kBulkMaxPart;
   if (part < 1) return MSHIFT_EUNSUPPORTED;
   const int parts = (args.tile_tokens + part - 1) / part;
   const int64_t items = (int64_t)args.tiles_per_layer * args.n_layers * parts;
   if (items > INT32_MAX) return MSHIFT_EUNSUPPORTED;
-  const int smem = static_cast<int>(kBulkStages * part * row_bytes);
+  const int smem = static_cast<int>(v->bulk_stages * part * row_bytes);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -971,8 +1032,10 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   a.k_scales = save ? nullptr : k_scales;
   a.err = err;
   const int64_t row_elems = (int64_t)paged->heads * 2 * paged->head_size;
-  if (!save && g_load_kernel.load(std::memory_order_relaxed) == MSHIFT_KERNEL_BULK &&
-      st_head == 2 * paged->head_size && st_tok == row_elems) {
+  const int kind = g_load_kernel.load(std::memory_order_relaxed);
+  const bool want_bulk =
+      kind == MSHIFT_KERNEL_BULK || (kind == MSHIFT_KERNEL_AUTO && paged->dtype == MSHIFT_E4M3);
+  if (!save && want_bulk && st_head == 2 * paged->head_size && st_tok == row_elems) {
     const int st = launch_bulk(v, a, row_elems * es, static_cast<cudaStream_t>(stream));
     if (st != MSHIFT_EUNSUPPORTED) return st;
   }
@@ -1103,7 +1166,8 @@ int mshift_supported(int32_t dtype, int32_t head_size, int32_t rotary) {
 }
 
 int mshift_set_load_kernel(int kind) {
-  if (kind != MSHIFT_KERNEL_LSU && kind != MSHIFT_KERNEL_BULK) return -1;
+  if (kind != MSHIFT_KERNEL_LSU && kind != MSHIFT_KERNEL_BULK && kind != MSHIFT_KERNEL_AUTO)
+    return -1;
   return g_load_kernel.exchange(kind);
 }
 

@@ -140,12 +140,13 @@ def rope_shift(delta: int, head_size: int, inv_freq: torch.Tensor, device) -> Ro
 
 
 def set_load_kernel(kind: str) -> str:
-    """Select the load kernel process-wide: ``"lsu"`` (default) or ``"bulk"`` (TMA).
+    """Select the load kernel process-wide: ``"auto"`` (default), ``"lsu"`` or ``"bulk"``.
 
-    Returns the previous selection.  Both write identical bits; they differ in
-    how the store rows reach the SM (128-bit loads vs one bulk copy per tile).
+    Returns the previous selection.  All write identical bits; they differ in
+    how the store rows reach the SM (128-bit loads vs one TMA bulk copy per
+    stage).  ``"auto"`` uses TMA for e4m3 caches and 128-bit loads otherwise.
     """
-    codes = {"lsu": _lib.KERNEL_LSU, "bulk": _lib.KERNEL_BULK}
+    codes = {"lsu": _lib.KERNEL_LSU, "bulk": _lib.KERNEL_BULK, "auto": _lib.KERNEL_AUTO}
     if kind not in codes:
         raise ShiftError(f"unknown load kernel {kind!r}")
     prev = _lib.load().mshift_set_load_kernel(codes[kind])
@@ -374,6 +375,7 @@ class Prepared:
     deltas: int
     n_deltas: int
     h2d_bytes: int
+    tile_tokens: int = 0
     tables: torch.Tensor | None = None
     k_scales: torch.Tensor | None = None
     inv_freq: torch.Tensor | None = None
@@ -395,11 +397,28 @@ class Launcher:
         self.geo: PagedLayout = layers.geometry
         self.device = layers.device
         self.lib = _lib.load()
+        self.fixed_tile = tile_tokens is not None and tile_tokens > 0
         self.tile_tokens = int(tile_tokens or self.lib.mshift_default_tile_tokens(self.geo.heads))
         self.paged = self.geo.struct()
         self.staging = _Staging(self.device)
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
+
+    #: tiles per resident CTA below which the launch's last wave is trimmed
+    MIN_TILES_PER_CTA = 48
+    #: a device's resident CTAs of the load/save kernel (148 SMs x 2 on B200)
+    RESIDENT_CTAS = 296
+
+    def _tile_for(self, tokens: int, n_layers: int) -> int:
+        """Tokens per tile: 256 (token, head) units, halved (down to 64 units) while the
+        launch would give each resident CTA fewer than MIN_TILES_PER_CTA tiles, so
+        the final wave of a short launch (one head per rank) stays small."""
+        heads = self.geo.heads
+        tt = max(1, int(self.lib.mshift_default_tile_tokens(heads)))
+        floor = max(1, 64 // heads)
+        while tt > floor and -(-tokens // tt) * n_layers < self.MIN_TILES_PER_CTA * self.RESIDENT_CTAS:
+            tt //= 2
+        return max(tt, floor)
 
     # -- packing ------------------------------------------------------------
     def _prepare(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
@@ -407,57 +426,65 @@ class Launcher:
         S, L = store.ptrs.shape
         if L != n_layers:
             raise ShiftError(f"store view has {L} layers, the launch covers {n_layers}")
-        host_tables: list[tuple[int, np.ndarray]] = []
-        for i, r in enumerate(runs):
-            if r.slots is None and r.block_table is not None and not isinstance(
-                r.block_table, torch.Tensor
-            ):
-                host_tables.append((i, np.ascontiguousarray(r.block_table, dtype=np.int32)))
+        length = np.fromiter((r.length for r in runs), dtype=np.int64, count=n_runs)
+        session = np.fromiter((r.session for r in runs), dtype=np.int64, count=n_runs)
+        if n_runs and (length.min() <= 0 or session.min() < 0 or session.max() >= S):
+            bad = int(np.argmax((length <= 0) | (session < 0) | (session >= S)))
+            raise ShiftError(f"run {bad}: length {length[bad]}, session row {session[bad]} of {S}")
+        tt = self.tile_tokens if self.fixed_tile else self._tile_for(int(length.sum()), n_layers)
+        self.tile_tokens = tt
+        ntiles = (length + tt - 1) // tt
+        tile_begin = np.zeros(n_runs, dtype=np.int64)
+        if n_runs > 1:
+            np.cumsum(ntiles[:-1], out=tile_begin[1:])
+        tiles = int(ntiles.sum())
+        if tiles * n_layers > 2**31 - 1:
+            raise ShiftError("batch too large for one launch")
+
+        # host block tables travel inside the staging copy, once per distinct table
+        host_tables: dict[int, np.ndarray] = {}
+        for r in runs:
+            bt = r.block_table
+            if r.slots is None and bt is not None and not isinstance(bt, torch.Tensor):
+                if id(bt) not in host_tables:
+                    host_tables[id(bt)] = np.ascontiguousarray(bt, dtype=np.int32)
         o_runs = 16
         o_ptrs = _align(o_runs + RUN_DTYPE.itemsize * n_runs)
         o_caps = _align(o_ptrs + 8 * S * L)
         o_deltas = _align(o_caps + 8 * S)
-        o_tabs = _align(o_deltas + 8 * max(len(deltas), 1))
-        tab_at, at = {}, o_tabs
-        for i, bt in host_tables:
-            tab_at[i] = at
+        tab_at, at = {}, _align(o_deltas + 8 * max(len(deltas), 1))
+        for key, bt in host_tables.items():
+            tab_at[key] = at
             at = _align(at + bt.nbytes)
         total = at
 
         slot, host, base = self.staging.begin(total)
         rec = np.zeros(n_runs, dtype=RUN_DTYPE)
-        tiles = 0
-        tt = self.tile_tokens
+        rec["store_start"] = np.fromiter((r.store_start for r in runs), dtype=np.int64,
+                                         count=n_runs)
+        rec["len"] = length
+        rec["session"] = session
+        rec["tile_begin"] = tile_begin
         table_of = {d: i for i, d in enumerate(deltas)}
+        rec["table"] = [table_of.get(int(r.delta), -1) for r in runs]
         for i, r in enumerate(runs):
-            if r.length <= 0:
-                raise ShiftError(f"run {i} has length {r.length}")
-            if not 0 <= r.session < S:
-                raise ShiftError(f"run {i} names session row {r.session} of {S}")
-            rec[i]["store_start"] = r.store_start
-            rec[i]["len"] = r.length
-            rec[i]["session"] = r.session
-            rec[i]["table"] = table_of[int(r.delta)] if int(r.delta) in table_of else -1
-            rec[i]["tile_begin"] = tiles
-            tiles += -(-r.length // tt)
             if r.slots is not None:
                 if r.slots.dtype != torch.int64 or not r.slots.is_cuda or r.slots.numel() < r.length:
                     raise ShiftError(f"run {i}: slots must be a CUDA int64 tensor of >= {r.length}")
                 rec[i]["slots"] = r.slots.data_ptr()
-            elif r.block_table is not None:
-                if isinstance(r.block_table, torch.Tensor):
-                    if r.block_table.dtype != torch.int32 or not r.block_table.is_cuda:
-                        raise ShiftError(f"run {i}: a tensor block_table must be CUDA int32")
-                    rec[i]["block_table"] = r.block_table.data_ptr()
-                    rec[i]["block_table_len"] = r.block_table.numel()
-                else:
-                    rec[i]["block_table"] = base + tab_at[i]
-                    rec[i]["block_table_len"] = len(r.block_table)
-                rec[i]["paged_start"] = r.paged_start
-            else:
+                continue
+            bt = r.block_table
+            if bt is None:
                 raise ShiftError(f"run {i} has neither slots nor a block table")
-        if tiles * n_layers > 2**31 - 1:
-            raise ShiftError("batch too large for one launch")
+            if isinstance(bt, torch.Tensor):
+                if bt.dtype != torch.int32 or not bt.is_cuda:
+                    raise ShiftError(f"run {i}: a tensor block_table must be CUDA int32")
+                rec[i]["block_table"] = bt.data_ptr()
+                rec[i]["block_table_len"] = bt.numel()
+            else:
+                rec[i]["block_table"] = base + tab_at[id(bt)]
+                rec[i]["block_table_len"] = host_tables[id(bt)].size
+            rec[i]["paged_start"] = r.paged_start
 
         host[:16] = 0  # the error word
         host[o_runs : o_runs + rec.nbytes] = rec.view(np.uint8)
@@ -471,13 +498,13 @@ class Launcher:
             host[o_deltas : o_deltas + 8 * len(deltas)] = np.asarray(deltas, dtype=np.int64).view(
                 np.uint8
             )
-        for i, bt in host_tables:
-            host[tab_at[i] : tab_at[i] + bt.nbytes] = bt.view(np.uint8)
+        for key, bt in host_tables.items():
+            host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
         self.staging.upload(slot, total)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
-                        base + o_deltas, len(deltas), total)
+                        base + o_deltas, len(deltas), total, tt)
 
     def prepare_load(
         self,
@@ -528,7 +555,7 @@ class Launcher:
             if main:
                 _lib.check(
                     self.lib.mshift_load(
-                        ctypes.byref(self.paged), 2 * half, p.runs, p.n_runs, self.tile_tokens,
+                        ctypes.byref(self.paged), 2 * half, p.runs, p.n_runs, p.tile_tokens,
                         p.tiles, p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
                         self.layers.k_ptrs.data_ptr(), self.layers.v_ptrs.data_ptr(),
                         p.tables.data_ptr() if p.tables is not None else None, p.n_deltas,
@@ -543,7 +570,7 @@ class Launcher:
                 off = 8 * p.first_layer
                 _lib.check(
                     self.lib.mshift_save(
-                        ctypes.byref(self.paged), p.runs, p.n_runs, self.tile_tokens, p.tiles,
+                        ctypes.byref(self.paged), p.runs, p.n_runs, p.tile_tokens, p.tiles,
                         p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
                         self.layers.k_ptrs.data_ptr() + off, self.layers.v_ptrs.data_ptr() + off,
                         p.base, stream,

@@ -103,6 +103,10 @@ class ShiftStore:
         self.device = device
         self.allocate = allocate
         self._sessions: OrderedDict[str, _Entry] = OrderedDict()  # oldest first
+        # bumped whenever a buffer is created, replaced or dropped: the cached
+        # pointer view handed to the native kernels is valid while it is unchanged
+        self._version = 0
+        self._view_cache: tuple | None = None
         self.hits = 0
         self.misses = 0
         self.evictions = 0
@@ -142,6 +146,7 @@ class ShiftStore:
             self.drop(victim)
             self.evictions += 1
         keep = entry.filled
+        self._version += 1
         for name, old in list(entry.layers.items()):
             fresh = torch.zeros((new_cap, *old.shape[1:]), dtype=old.dtype, device=old.device)
             n = min(keep, old.shape[0])
@@ -215,7 +220,8 @@ class ShiftStore:
         return buf[start : start + n]
 
     def drop(self, session: str) -> None:
-        self._sessions.pop(session, None)
+        if self._sessions.pop(session, None) is not None:
+            self._version += 1
 
     def stats(self) -> dict:
         return {
@@ -242,6 +248,7 @@ class ShiftStore:
         if buf is None:
             buf = torch.zeros((entry.capacity, *row_shape), dtype=dtype, device=self.device)
             entry.layers[layer] = buf
+            self._version += 1
         return buf
 
     def ensure_layers(
@@ -262,15 +269,21 @@ class ShiftStore:
         reference's per-layer ``read`` discovered a gap mid-loop.
         """
         entry = self._readable(session, start, n)
+        if entry is not None and entry.layers.keys() >= set(layers):
+            return None
         for name in layers:
             if entry is None or name not in entry.layers:
                 return name
         return None
 
     def mark_loaded(self, session: str, layers: list[str], n: int) -> None:
-        """Counters and LRU touches of one ``read`` per layer (``shift_store.py:245-249``)."""
-        for _ in layers:
-            self.loaded_token_layers += n
+        """Counters and LRU position after one ``read`` per layer (``shift_store.py:245-249``).
+
+        Touching the same session once or once per layer leaves the same LRU
+        order, so it is touched once.
+        """
+        self.loaded_token_layers += n * len(layers)
+        if layers:
             self._touch(session)
 
     def adopt(self, session: str, layers: dict[str, torch.Tensor], base: int, filled: int) -> None:
@@ -286,6 +299,7 @@ class ShiftStore:
         entry.capacity = caps.pop()
         entry.base, entry.filled = int(base), int(filled)
         entry.layers = dict(layers)
+        self._version += 1
 
     def mark_saved(self, n_tokens: int, n_layers: int) -> None:
         self.saved_token_layers += n_tokens * n_layers
@@ -302,6 +316,10 @@ class ShiftStore:
         """
         from .shift_kernels import StoreView
 
+        key = (tuple(sessions), tuple(layers))
+        cached = self._view_cache
+        if cached is not None and cached[0] == key and cached[1] == self._version:
+            return cached[2]
         ptrs = np.zeros((len(sessions), len(layers)), dtype=np.uint64)
         caps = np.zeros(len(sessions), dtype=np.int64)
         st_tok = st_head = None
@@ -321,7 +339,9 @@ class ShiftStore:
                     st_tok, st_head = buf.stride(0), buf.stride(1)
                 elif (st_tok, st_head) != (buf.stride(0), buf.stride(1)):
                     raise ValueError("store buffers of one batch must share a row layout")
-        return StoreView(ptrs, caps, st_tok or 0, st_head or 0, keep)
+        view = StoreView(ptrs, caps, st_tok or 0, st_head or 0, keep)
+        self._view_cache = (key, self._version, view)
+        return view
 
 
 @dataclass(frozen=True)

@@ -286,11 +286,11 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._blocks[rid] = list(req.block_ids[0])
             session = self._table.session_of(rid) or ""
             if rid in self._need_load and rid in self._multi:
+                table = list(self._blocks[rid])  # one block table shared by the segments
                 for seg in self._multi[rid]:
                     n = seg["dst_end"] - seg["dst_start"]
                     meta.loads.append(_Load(session, seg["dst_start"] - seg["delta"],
-                                            seg["delta"], seg["dst_start"], n,
-                                            list(self._blocks[rid]), self._bs))
+                                            seg["delta"], seg["dst_start"], n, table, self._bs))
                 self._need_load.discard(rid)
             elif rid in self._need_load:
                 lo, hi, delta = self._plans[rid]

@@ -57,11 +57,16 @@ class SaveJob:
     slots: torch.Tensor | None = None
 
 
-def _run(row: int, store_start: int, length: int, delta: int, block_ids, slots, paged_start):
+def _run(row: int, store_start: int, length: int, delta: int, block_ids, slots, paged_start,
+         tables: dict):
+    """A RunSpec; jobs that share one block-table object share one converted table."""
     if slots is not None:
         return RunSpec(row, store_start, length, delta, slots=slots)
-    return RunSpec(row, store_start, length, delta, block_table=np.asarray(block_ids, np.int32),
-                   paged_start=paged_start)
+    key = id(block_ids)
+    bt = tables.get(key)
+    if bt is None:
+        bt = tables[key] = np.asarray(block_ids, np.int32)
+    return RunSpec(row, store_start, length, delta, block_table=bt, paged_start=paged_start)
 
 
 class ShiftWorker:
@@ -126,10 +131,11 @@ class ShiftWorker:
             return []
         rows: dict[str, int] = {}
         runs = []
+        tables: dict = {}
         for job in accepted:
             row = rows.setdefault(job.session, len(rows))
             runs.append(_run(row, job.src_start, job.length, job.delta, job.block_ids, job.slots,
-                             job.dst_start))
+                             job.dst_start, tables))
         view = self.store.view(list(rows), names)
         self.launcher.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
         return accepted
@@ -156,6 +162,7 @@ class ShiftWorker:
         dtype = self.layers.tensors[0].dtype
         rows: dict[str, int] = {}
         runs = []
+        tables: dict = {}
         for job in jobs:
             if not self.store.ensure_layers(job.session, names, geo.heads, 2 * geo.head_size,
                                             dtype):
@@ -164,7 +171,7 @@ class ShiftWorker:
                 continue
             row = rows.setdefault(job.session, len(rows))
             runs.append(_run(row, job.dst_start, job.length, 0, job.block_ids, job.slots,
-                             job.dst_start))
+                             job.dst_start, tables))
         if not runs:
             return 0
         view = self.store.view(list(rows), names)

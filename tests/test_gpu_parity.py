@@ -59,7 +59,11 @@ def inv128():
 
 @pytest.fixture(params=["lsu", "bulk"])
 def load_kernel(request, cuda):
-    """Run a batched-load test through each load kernel (128-bit loads / TMA bulk)."""
+    """Run a batched-load test through each load kernel (128-bit loads / TMA bulk).
+
+    The process default ("auto") picks one of the two per dtype; forcing each
+    covers both for every case.
+    """
     prev = sk.set_load_kernel(request.param)
     yield request.param
     sk.set_load_kernel(prev)
