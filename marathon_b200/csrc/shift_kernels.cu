@@ -152,38 +152,31 @@ struct E4m3 {
   }
 };
 
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b);
-
-// e4m3 codes of (r.x / s, r.y / s), each exactly the saturating
-// round-to-nearest-even of the correctly rounded quotient __fdiv_rn(r, s).
-// q = r * (1/s) is within 2.5 ulp of that quotient.  Converting q*(1-2^-21)
-// and q*(1+2^-21) (an interval of at least 4 ulp on each side of q) gives the
-// same code for both ends exactly when every value in between, the quotient
-// included, rounds to that code (the conversion is monotonic); only when the
-// ends differ -- q sits next to an e4m3 rounding boundary -- is the quotient
-// formed by division.
-__device__ __forceinline__ uint32_t requant2(float2 r, float s, float inv) {
-  const float2 q = mul2_rn(r, make_float2(inv, inv));
-  const float2 lo = mul2_rn(q, make_float2(0.99999952316284180f, 0.99999952316284180f));
-  const float2 hi = mul2_rn(q, make_float2(1.00000047683715820f, 1.00000047683715820f));
-  const uint32_t c_lo = __nv_cvt_float2_to_fp8x2(lo, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
-  const uint32_t c_hi = __nv_cvt_float2_to_fp8x2(hi, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
-  if (c_lo == c_hi) return c_lo;
-  const float2 exact = make_float2(__fdiv_rn(r.x, s), __fdiv_rn(r.y, s));
-  return __nv_cvt_float2_to_fp8x2(exact, __NV_SATFINITE, __NV_E4M3) & 0xffffu;
+// e4m3 codes of r[k] / s (four values, one 32-bit word), each exactly the
+// saturating round-to-nearest-even of the correctly rounded quotient
+// __fdiv_rn(r, s).  q = r * (1/s) is within 2.5 ulp of that quotient.
+// Converting q*(1-2^-21) and q*(1+2^-21) (at least 3.5 ulp on each side of q)
+// gives the same codes for both ends exactly when every value in between, the
+// quotient included, rounds to those codes (the conversion is monotonic).
+// Only when some end differs -- a value sits next to an e4m3 rounding
+// boundary -- are the quotients formed by division; the test is voted across
+// the warp so that rare path is taken by whole warps.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float2 v) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3));
 }
 
-// Packed fp32x2 multiply, each lane rounded to nearest.  Measured on B200
-// (sm_100a, CUDA 12.9): a packed multiply feeding a packed add was fused into
-// an FMA even with explicit .rn modifiers, so the adds that follow stay scalar
-// (__fadd_rn / __fsub_rn are never merged with a multiply).
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  float2 r;
-  asm("{\n\t.reg .b64 pa, pb, pd;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
-      "mul.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return r;
+__device__ __forceinline__ uint32_t requant4(const float2* r, float s, float inv) {
+  const float2 i2 = make_float2(inv, inv);
+  const float2 dn = make_float2(0.99999952316284180f, 0.99999952316284180f);  // 1 - 2^-21
+  const float2 up = make_float2(1.00000047683715820f, 1.00000047683715820f);  // 1 + 2^-21
+  const float2 q0 = __fmul2_rn(r[0], i2), q1 = __fmul2_rn(r[1], i2);
+  const uint32_t lo = cvt_e4m3x2(__fmul2_rn(q0, dn)) | (cvt_e4m3x2(__fmul2_rn(q1, dn)) << 16);
+  const uint32_t hi = cvt_e4m3x2(__fmul2_rn(q0, up)) | (cvt_e4m3x2(__fmul2_rn(q1, up)) << 16);
+  if (!__any_sync(__activemask(), lo != hi)) return lo;
+  if (lo == hi) return lo;
+  const float2 e0 = make_float2(__fdiv_rn(r[0].x, s), __fdiv_rn(r[0].y, s));
+  const float2 e1 = make_float2(__fdiv_rn(r[1].x, s), __fdiv_rn(r[1].y, s));
+  return cvt_e4m3x2(e0) | (cvt_e4m3x2(e1) << 16);
 }
 
 // Rotate one pair of partner vectors in place: `a` holds elements
@@ -199,10 +192,37 @@ __device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, con
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     float x[P], y[P];
-    uint32_t qa = 0, qb = 0;  // requantised codes (scaled types)
     E::unpack(a.w[w], x);
     E::unpack(b.w[w], y);
-    if constexpr (P == 1) {
+    if constexpr (E::kScaled) {
+      // e4m3: four elements per word; cos/sin as float4; one requantisation
+      // test per word, taken warp-uniformly
+      const float4 c4 = *reinterpret_cast<const float4*>(cs + 4 * w);
+      const float4 s4 = *reinterpret_cast<const float4*>(sn + 4 * w);
+      const float2 sc = make_float2(scale, scale);
+      const float2 c01 = make_float2(c4.x, c4.y), c23 = make_float2(c4.z, c4.w);
+      const float2 s01 = make_float2(s4.x, s4.y), s23 = make_float2(s4.z, s4.w);
+      const float2 x01 = __fmul2_rn(make_float2(x[0], x[1]), sc);
+      const float2 x23 = __fmul2_rn(make_float2(x[2], x[3]), sc);
+      const float2 y01 = __fmul2_rn(make_float2(y[0], y[1]), sc);
+      const float2 y23 = __fmul2_rn(make_float2(y[2], y[3]), sc);
+      float2 ra[2], rb[2];
+      {
+        const float2 xc = __fmul2_rn(x01, c01), ys = __fmul2_rn(y01, s01);
+        const float2 yc = __fmul2_rn(y01, c01), xs = __fmul2_rn(x01, s01);
+        ra[0] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+        rb[0] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+      }
+      {
+        const float2 xc = __fmul2_rn(x23, c23), ys = __fmul2_rn(y23, s23);
+        const float2 yc = __fmul2_rn(y23, c23), xs = __fmul2_rn(x23, s23);
+        ra[1] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+        rb[1] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+      }
+      a.w[w] = requant4(ra, scale, inv_scale);
+      b.w[w] = requant4(rb, scale, inv_scale);
+      continue;
+    } else if constexpr (P == 1) {
       const float c = cs[w], s = sn[w];
       float xe = x[0], ye = y[0];
       if constexpr (E::kScaled) {
@@ -216,35 +236,20 @@ __device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, con
       for (int j = 0; j < P / 2; ++j) {
         const float2 c = *reinterpret_cast<const float2*>(cs + P * w + 2 * j);
         const float2 s = *reinterpret_cast<const float2*>(sn + P * w + 2 * j);
-        float2 x2 = make_float2(x[2 * j], x[2 * j + 1]);
-        float2 y2 = make_float2(y[2 * j], y[2 * j + 1]);
-        if constexpr (E::kScaled) {
-          const float2 sc = make_float2(scale, scale);
-          x2 = mul2_rn(x2, sc);
-          y2 = mul2_rn(y2, sc);
-        }
+        const float2 x2 = make_float2(x[2 * j], x[2 * j + 1]);
+        const float2 y2 = make_float2(y[2 * j], y[2 * j + 1]);
         // packed products, scalar adds: __fadd_rn / __fsub_rn are never merged
         // with a multiply, so every product is rounded before it is added
-        const float2 xc = mul2_rn(x2, c), ys = mul2_rn(y2, s);
-        const float2 yc = mul2_rn(y2, c), xs = mul2_rn(x2, s);
+        const float2 xc = __fmul2_rn(x2, c), ys = __fmul2_rn(y2, s);
+        const float2 yc = __fmul2_rn(y2, c), xs = __fmul2_rn(x2, s);
         const float2 ra = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
         const float2 rb = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-        if constexpr (E::kScaled) {
-          qa |= requant2(ra, scale, inv_scale) << (16 * j);
-          qb |= requant2(rb, scale, inv_scale) << (16 * j);
-        } else {
-          x[2 * j] = ra.x, x[2 * j + 1] = ra.y;
-          y[2 * j] = rb.x, y[2 * j + 1] = rb.y;
-        }
+        x[2 * j] = ra.x, x[2 * j + 1] = ra.y;
+        y[2 * j] = rb.x, y[2 * j + 1] = rb.y;
       }
     }
-    if constexpr (E::kScaled) {
-      a.w[w] = qa;
-      b.w[w] = qb;
-    } else {
-      a.w[w] = E::pack(x);
-      b.w[w] = E::pack(y);
-    }
+    a.w[w] = E::pack(x);
+    b.w[w] = E::pack(y);
   }
 }
 
@@ -494,7 +499,7 @@ __host__ __device__ constexpr int bulk_stage_bytes() {
 }
 constexpr int kBulkMaxStages = 8;
 constexpr int kBulkMaxPart = 128;          // tokens per stage, upper bound
-constexpr uint32_t kWaitLimit = 1u << 22;  // try_wait rounds before giving up
+constexpr uint32_t kWaitLimit = 1u << 18;  // try_wait rounds before giving up (seconds)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -515,14 +520,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// One try_wait round: the thread may sleep up to kWaitHintNs for the phase to
+// complete instead of spinning (fewer issue slots spent waiting).
+constexpr uint32_t kWaitHintNs = 20000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kWaitHintNs)
       : "memory");
   return done != 0;
 }
