@@ -160,8 +160,17 @@ class CpuPath:
         inv = O.inv_freq(d, cfg.theta)
         self.emb = T.emb_tables(torch.from_numpy(O.rope_tables([seg.delta], inv)[0]))
         g = torch.Generator().manual_seed(0)
-        self.srcs = [torch.randn(self.n, h, 2 * d, generator=g).to(torch.bfloat16) for _ in range(2)]
-        self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.bfloat16) for _ in range(2)]
+        self.fp8 = cfg.dtype == "e4m3"
+        if self.fp8:  # codes of the c3 distribution: values / per-layer scale, saturated
+            self.k_scale = 0.05
+            self.srcs = [(torch.randn(self.n, h, 2 * d, generator=g) * 20).clamp(-448, 448)
+                         .to(torch.float8_e4m3fn) for _ in range(2)]
+            self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.float8_e4m3fn)
+                        for _ in range(2)]
+        else:
+            self.srcs = [torch.randn(self.n, h, 2 * d, generator=g).to(torch.bfloat16)
+                         for _ in range(2)]
+            self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.bfloat16) for _ in range(2)]
         self.bs = bs
         self.i = 0
         self.run(tokens=256)  # first touch
@@ -172,8 +181,12 @@ class CpuPath:
         k = self.i % 2
         self.i += 1
         t0 = time.perf_counter()
-        self.T.scatter_layer(self.srcs[k][:n], self.kvs[k], self.slots[:n], self.bs, False,
-                             self.emb)
+        if self.fp8:
+            self.T.scatter_layer_e4m3(self.srcs[k][:n], self.kvs[k], self.slots[:n], self.bs,
+                                      False, self.emb, self.k_scale)
+        else:
+            self.T.scatter_layer(self.srcs[k][:n], self.kvs[k], self.slots[:n], self.bs, False,
+                                 self.emb)
         return time.perf_counter() - t0, n * self.cfg.bytes_per_token_layer()
 
     def sample(self, seconds: float) -> dict:
@@ -187,8 +200,8 @@ class CpuPath:
         return {"gbs": moved / el / 1e9, "seconds": el, "layers": done,
                 "ms_per_layer": el / done * 1e3,
                 "sample": f"{done} layer(s) of {self.cfg.name}: {self.n} tokens x "
-                          f"{self.cfg.heads} heads x {2 * self.cfg.head_size} bf16 each, "
-                          f"torch CPU, {self.threads} threads"}
+                          f"{self.cfg.heads} heads x {2 * self.cfg.head_size} "
+                          f"{self.cfg.dtype} each, torch CPU, {self.threads} threads"}
 
 
 def reference_arm(args) -> None:
@@ -215,8 +228,8 @@ def reference_arm(args) -> None:
     line = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_turn, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "impl": "reference",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": cfg.dtype, "data": "synthetic", "impl": "reference",
         "config": {"workload": f"{cfg.name} {cfg.model} shift turn", "layers": cfg.layers,
                    "tokens_shifted": seg.length, "delta": seg.delta, "heads": cfg.heads,
                    "head_size": cfg.head_size, "block_size": cfg.block_size, "layout": "nhd",

@@ -23,6 +23,7 @@ status raises :class:`ShiftError`.
 from __future__ import annotations
 
 import ctypes
+import struct
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -296,6 +297,10 @@ class StoreView:
     st_head: int
     keepalive: list = field(default_factory=list, repr=False)
 
+    def __post_init__(self) -> None:
+        self.ptrs = np.ascontiguousarray(self.ptrs, dtype=np.uint64)
+        self.caps = np.ascontiguousarray(self.caps, dtype=np.int64)
+
 
 def _align(n: int, a: int = 16) -> int:
     return (n + a - 1) // a * a
@@ -327,7 +332,9 @@ class _Staging:
                 ev.synchronize()
         cap = 1 << max(12, (n - 1).bit_length())
         self.host = [torch.empty(cap, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.host_np = [h.numpy() for h in self.host]
         self.dev = [torch.empty(cap, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        self.dev_ptr = [d.data_ptr() for d in self.dev]
         self.done = [None, None]
         self.cap = cap
 
@@ -339,7 +346,7 @@ class _Staging:
         ev = self.done[slot]
         if ev is not None:
             ev.synchronize()
-        return slot, self.host[slot].numpy(), self.dev[slot].data_ptr()
+        return slot, self.host_np[slot], self.dev_ptr[slot]
 
     def upload(self, slot: int, n: int) -> None:
         self.dev[slot][:n].copy_(self.host[slot][:n], non_blocking=True)
@@ -403,6 +410,7 @@ class Launcher:
         self.staging = _Staging(self.device)
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
+        self._tables: list[torch.Tensor | None] = [None, None]
 
     #: tiles per resident CTA below which the launch's last wave is trimmed
     MIN_TILES_PER_CTA = 48
@@ -421,7 +429,12 @@ class Launcher:
         return max(tt, floor)
 
     # -- packing ------------------------------------------------------------
+    _RUN = struct.Struct("<qqQQiiiiii")  # mshift_run, 56 bytes
+    _SMALL = 32  # batches up to this many runs are packed record by record
+
     def _prepare(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
+        if len(runs) <= self._SMALL:
+            return self._prepare_small(kind, runs, store, deltas, first_layer, n_layers)
         n_runs = len(runs)
         S, L = store.ptrs.shape
         if L != n_layers:
@@ -506,6 +519,75 @@ class Launcher:
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
                         base + o_deltas, len(deltas), total, tt)
 
+    def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
+        """``_prepare`` for a few runs: records packed straight into the pinned slot."""
+        n_runs = len(runs)
+        S, L = store.ptrs.shape
+        if L != n_layers:
+            raise ShiftError(f"store view has {L} layers, the launch covers {n_layers}")
+        total_tokens = 0
+        for i, r in enumerate(runs):
+            if r.length <= 0 or not 0 <= r.session < S:
+                raise ShiftError(f"run {i}: length {r.length}, session row {r.session} of {S}")
+            total_tokens += r.length
+        tt = self.tile_tokens if self.fixed_tile else self._tile_for(total_tokens, n_layers)
+        self.tile_tokens = tt
+        host_tables: dict[int, np.ndarray] = {}
+        for r in runs:
+            bt = r.block_table
+            if r.slots is None and bt is not None and not isinstance(bt, torch.Tensor):
+                if id(bt) not in host_tables:
+                    host_tables[id(bt)] = np.ascontiguousarray(bt, dtype=np.int32)
+        o_runs = 16
+        o_ptrs = _align(o_runs + 56 * n_runs)
+        o_caps = _align(o_ptrs + 8 * S * L)
+        o_deltas = _align(o_caps + 8 * S)
+        tab_at, at = {}, _align(o_deltas + 8 * max(len(deltas), 1))
+        for key, bt in host_tables.items():
+            tab_at[key] = at
+            at = _align(at + bt.nbytes)
+        total = at
+        slot, host, base = self.staging.begin(total)
+        table_of = {d: i for i, d in enumerate(deltas)}
+        pack = self._RUN.pack_into
+        tiles = 0
+        for i, r in enumerate(runs):
+            slots_ptr = bt_ptr = 0
+            bt_len = 0
+            paged_start = 0
+            if r.slots is not None:
+                if r.slots.dtype != torch.int64 or not r.slots.is_cuda or r.slots.numel() < r.length:
+                    raise ShiftError(f"run {i}: slots must be a CUDA int64 tensor of >= {r.length}")
+                slots_ptr = r.slots.data_ptr()
+            else:
+                bt = r.block_table
+                if bt is None:
+                    raise ShiftError(f"run {i} has neither slots nor a block table")
+                if isinstance(bt, torch.Tensor):
+                    if bt.dtype != torch.int32 or not bt.is_cuda:
+                        raise ShiftError(f"run {i}: a tensor block_table must be CUDA int32")
+                    bt_ptr, bt_len = bt.data_ptr(), bt.numel()
+                else:
+                    bt_ptr, bt_len = base + tab_at[id(bt)], host_tables[id(bt)].size
+                paged_start = r.paged_start
+            pack(host, o_runs + 56 * i, r.store_start, paged_start, slots_ptr, bt_ptr, bt_len,
+                 r.length, r.session, table_of.get(int(r.delta), -1), tiles, 0)
+            tiles += -(-r.length // tt)
+        if tiles * n_layers > 2**31 - 1:
+            raise ShiftError("batch too large for one launch")
+        host[:16] = 0  # the error word
+        host[o_ptrs : o_ptrs + 8 * S * L] = store.ptrs.view(np.uint8).reshape(-1)
+        host[o_caps : o_caps + 8 * S] = store.caps.view(np.uint8)
+        for k, d in enumerate(deltas):
+            struct.pack_into("<q", host, o_deltas + 8 * k, d)
+        for key, bt in host_tables.items():
+            host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
+        self.staging.upload(slot, total)
+        self.last_h2d = total
+        return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
+                        base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
+                        base + o_deltas, len(deltas), total, tt)
+
     def prepare_load(
         self,
         runs: list[RunSpec],
@@ -523,11 +605,16 @@ class Launcher:
             if k_scales.numel() < len(self.layers):
                 raise ShiftError("need one K scale per layer")
         p = self._prepare("load", runs, store, deltas, 0, len(self.layers))
-        p.inv_freq = inv_freq.to(torch.float32).contiguous()
+        p.inv_freq = inv_freq if inv_freq.dtype == torch.float32 else inv_freq.float()
         p.k_scales = k_scales if deltas else None
         if deltas:
-            p.tables = torch.empty((len(deltas), 2, p.inv_freq.numel()), dtype=torch.float32,
-                                   device=self.device)
+            # per staging slot, so a batch still in flight keeps its tables
+            need = len(deltas) * 2 * p.inv_freq.numel()
+            buf = self._tables[p.slot]
+            if buf is None or buf.numel() < need:
+                buf = torch.empty(max(need, 1024), dtype=torch.float32, device=self.device)
+                self._tables[p.slot] = buf
+            p.tables = buf
         return p
 
     def prepare_save(

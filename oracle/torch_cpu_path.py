@@ -49,3 +49,28 @@ def load_layers(srcs, kvs, slots, block_size: int, hnd: bool, emb) -> None:
     """The connector's per-layer loop over one load."""
     for src, kv in zip(srcs, kvs, strict=True):
         scatter_layer(src, kv, slots, block_size, hnd, emb)
+
+
+def scatter_layer_e4m3(src, kv, slots, block_size: int, hnd: bool, emb, k_scale: float) -> None:
+    """The same layer for e4m3 codes: dequantise with ``k_scale``, rotate, divide by it,
+    saturate to +-448, round to e4m3; V codes copied.  ``src``/``kv`` are
+    ``torch.float8_e4m3fn`` tensors (the reference has no scale handling; this is
+    the requantisation the build defines for FP8 caches).
+    """
+    d = src.shape[-1] // 2
+    k = src[..., :d]
+    if emb is not None:
+        emb_cos, emb_sin = emb
+        kf = k.to(torch.float32) * k_scale
+        h = kf.shape[-1] // 2
+        turned = torch.cat((-kf[..., h:], kf[..., :h]), dim=-1)
+        r = kf * emb_cos + turned * emb_sin
+        k = (r / k_scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    blk = torch.div(slots, block_size, rounding_mode="floor")
+    off = slots - blk * block_size
+    rows = torch.cat((k.view(torch.uint8), src[..., d:].view(torch.uint8)), dim=-1)
+    target = kv.view(torch.uint8)
+    if hnd:
+        target[blk, :, off] = rows
+    else:
+        target[blk, off] = rows

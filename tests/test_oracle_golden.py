@@ -246,3 +246,21 @@ def test_save_then_unshifted_load_is_identity():
     k, v = paged.read(idx)
     k0, v0 = O.Paged(flat, 0, d, bs * heads * 2 * d, heads * 2 * d, 2 * d, bs, heads, d).read(idx)
     assert np.array_equal(k, k0) and np.array_equal(v, v0)
+
+
+def test_torch_cpu_e4m3_path_equals_the_numpy_oracle(golden):
+    """The e4m3 CPU baseline (dequantise, rotate, divide, saturate) is the oracle, bit for bit."""
+    rng = np.random.default_rng(8)
+    n = 40
+    vals = (rng.standard_normal((n, HEADS, 2 * D)) * 60).clip(-448, 448).astype(np.float32)
+    codes = O.f32_to_e4m3(vals)
+    slots = golden["bf16_slots"]
+    tab = O.rope_tables([-566], golden["inv_freq_128_1000000"])[0]
+    k_scale = 0.0371
+    src = torch.from_numpy(codes.copy()).view(torch.float8_e4m3fn)
+    kv = torch.zeros((64, BS, HEADS, 2 * D), dtype=torch.float8_e4m3fn)
+    T.scatter_layer_e4m3(src, kv, torch.from_numpy(slots), BS, False,
+                         T.emb_tables(torch.from_numpy(tab)), k_scale)
+    paged = _flat_paged(False, 64, dtype=np.uint8)
+    O.scatter_shifted(codes, paged, slots, tab, O.E4M3, k_scale)
+    assert np.array_equal(kv.view(torch.uint8).numpy().reshape(-1), paged.flat)
