@@ -407,26 +407,37 @@ class Launcher:
         self.fixed_tile = tile_tokens is not None and tile_tokens > 0
         self.tile_tokens = int(tile_tokens or self.lib.mshift_default_tile_tokens(self.geo.heads))
         self.paged = self.geo.struct()
+        props = torch.cuda.get_device_properties(self.device)
+        self._grid = props.multi_processor_count * self.CTAS_PER_SM
         self.staging = _Staging(self.device)
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
         self._tables: list[torch.Tensor | None] = [None, None]
 
-    #: tiles per resident CTA below which the launch's last wave is trimmed
-    MIN_TILES_PER_CTA = 48
-    #: a device's resident CTAs of the load/save kernel (148 SMs x 2 on B200)
-    RESIDENT_CTAS = 296
+    #: resident CTAs of the load/save kernel per SM (register-limited, B200)
+    CTAS_PER_SM = 2
 
-    def _tile_for(self, tokens: int, n_layers: int) -> int:
-        """Tokens per tile: 256 (token, head) units, halved (down to 64 units) while the
-        launch would give each resident CTA fewer than MIN_TILES_PER_CTA tiles, so
-        the final wave of a short launch (one head per rank) stays small."""
+    #: per-tile cost in (token, head) units: barriers, slot resolution, table staging
+    TILE_OVERHEAD_UNITS = 16
+
+    def _tile_for(self, tokens: int, n_layers: int, lengths=None) -> int:
+        """Tokens per tile that balance the launch's last wave.
+
+        Tiles of 256 (token, head) units are the measured best; smaller tiles
+        pay per-tile overhead.  Between 128 and 256 units, pick the size that
+        minimises the most any CTA does: (tiles per CTA, rounded up) x (tile
+        units + per-tile overhead).  A short launch (one head per rank) gets a
+        tile count just under a multiple of the resident CTAs instead of a
+        last wave that leaves most of them idle.
+        """
         heads = self.geo.heads
-        tt = max(1, int(self.lib.mshift_default_tile_tokens(heads)))
-        floor = max(1, 64 // heads)
-        while tt > floor and -(-tokens // tt) * n_layers < self.MIN_TILES_PER_CTA * self.RESIDENT_CTAS:
-            tt //= 2
-        return max(tt, floor)
+        t_max = max(1, int(self.lib.mshift_default_tile_tokens(heads)))
+        t_min = max(1, t_max // 2)
+        lens = np.asarray([tokens] if lengths is None else lengths, dtype=np.int64)
+        cand = np.arange(t_max, t_min - 1, -1, dtype=np.int64)
+        tiles = n_layers * (-(-lens[:, None] // cand[None, :])).sum(axis=0)
+        cost = -(-tiles // self._grid) * (cand * heads + self.TILE_OVERHEAD_UNITS)
+        return int(cand[int(np.argmin(cost))])  # first minimum: the largest tile
 
     # -- packing ------------------------------------------------------------
     _RUN = struct.Struct("<qqQQiiiiii")  # mshift_run, 56 bytes
@@ -444,7 +455,8 @@ class Launcher:
         if n_runs and (length.min() <= 0 or session.min() < 0 or session.max() >= S):
             bad = int(np.argmax((length <= 0) | (session < 0) | (session >= S)))
             raise ShiftError(f"run {bad}: length {length[bad]}, session row {session[bad]} of {S}")
-        tt = self.tile_tokens if self.fixed_tile else self._tile_for(int(length.sum()), n_layers)
+        tt = self.tile_tokens if self.fixed_tile else self._tile_for(
+            int(length.sum()), n_layers, length.tolist() if n_runs <= 512 else None)
         self.tile_tokens = tt
         ntiles = (length + tt - 1) // tt
         tile_begin = np.zeros(n_runs, dtype=np.int64)
@@ -530,7 +542,8 @@ class Launcher:
             if r.length <= 0 or not 0 <= r.session < S:
                 raise ShiftError(f"run {i}: length {r.length}, session row {r.session} of {S}")
             total_tokens += r.length
-        tt = self.tile_tokens if self.fixed_tile else self._tile_for(total_tokens, n_layers)
+        tt = self.tile_tokens if self.fixed_tile else self._tile_for(
+            total_tokens, n_layers, [r.length for r in runs])
         self.tile_tokens = tt
         host_tables: dict[int, np.ndarray] = {}
         for r in runs:
