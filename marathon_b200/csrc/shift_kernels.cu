@@ -751,6 +751,10 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
   }
 
   // -------------------------------------------------------------- consumers
+  // e4m3 units are arithmetic-heavy: one unit in flight per thread, and the
+  // thread's cos/sin slice held in registers for the whole stage.
+  constexpr int U = E::kScaled ? 1 : 2;
+  constexpr bool kRegTable = E::kScaled;
   const int g = threadIdx.x % G;
   const int u_first = threadIdx.x / G;
   const int ka = g < NP ? g : g + NP;
@@ -767,13 +771,27 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
     const unsigned char* stage = s_data + s * stage_bytes;
     const int nu = m.nt * a.heads;
     const bool rotate = m.rotate && g < NP;
-    for (int u = u_first; u < nu; u += 2 * UPP) {
-      Vec kv[2][2], vv[2][2];
-      char* kp[2];
-      char* vp[2];
-      bool live[2];
+    float treg[kRegTable ? 2 * VEC : 4];
+    const float* tc = s_tab[s] + g * VEC;
+    const float* ts = s_tab[s] + HALF + g * VEC;
+    if constexpr (kRegTable) {
+      if (rotate) {
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+        for (int e = 0; e < VEC; e += 4) {
+          *reinterpret_cast<float4*>(treg + e) = *reinterpret_cast<const float4*>(tc + e);
+          *reinterpret_cast<float4*>(treg + VEC + e) = *reinterpret_cast<const float4*>(ts + e);
+        }
+      }
+      tc = treg;
+      ts = treg + VEC;
+    }
+    for (int u = u_first; u < nu; u += U * UPP) {
+      Vec kv[U][2], vv[U][2];
+      char* kp[U];
+      char* vp[U];
+      bool live[U];
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
         const int uu = u + q * UPP;
         live[q] = false;
         if (uu < nu) {
@@ -793,11 +811,9 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
         }
       }
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
-        if (rotate)
-          rotate_pair<E>(kv[q][0], kv[q][1], s_tab[s] + g * VEC, s_tab[s] + HALF + g * VEC,
-                         m.kscale, m.kinv);
+        if (rotate) rotate_pair<E>(kv[q][0], kv[q][1], tc, ts, m.kscale, m.kinv);
         store_vec(kp[q] + ka * 16, kv[q][0]);
         store_vec(kp[q] + kb * 16, kv[q][1]);
         store_vec(vp[q] + g * 16, vv[q][0]);
