@@ -323,7 +323,8 @@ def native_arm(args) -> None:
     if world > 1:
         dist.barrier(device_ids=[local])
     elapsed = start.elapsed_time(end)
-    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    per_step = [a.elapsed_time(b) for a, b in kev]
+    kernel_ms = statistics.mean(per_step)
     t = torch.tensor([elapsed], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -455,6 +456,8 @@ def native_arm(args) -> None:
                 "kernel": ("bulk_load_kernel (mshift_load, TMA)" if fp8
                            else "move_kernel<load> (mshift_load)"),
                 "kernel_ms": round(kernel_ms, 4),
+                "kernel_ms_best": round(min(per_step), 4),
+                "kernel_ms_median": round(statistics.median(per_step), 4),
                 "bytes_per_launch": rank_bytes,
                 "traffic": round(traffic) if traffic else None,
                 "alternatives": alt,
