@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (profiling cases)")
     ap.add_argument("--no-save", action="store_true", help="skip the save-kernel timing")
     ap.add_argument("--no-alt", action="store_true", help="skip the TMA bulk-load timing")
+    ap.add_argument("--no-host-tier", action="store_true",
+                    help="skip the pinned-host store tier timing (N=1 only)")
     return ap.parse_args()
 
 
@@ -246,6 +248,67 @@ def reference_arm(args) -> None:
 
 
 # ---------------------------------------------------------------- native
+def host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device) -> dict:
+    """The same turn from a store in pinned host memory, through staged copies.
+
+    Rows cross the host link once per step (copy engines into a device staging
+    ring, ``mshift_stage``), then the ordinary load kernel runs from staging.
+    The bound is the host-to-device copy bandwidth, measured here on one large
+    pinned copy.
+    """
+    from marathon_b200.shift_store import ShiftStore
+    from marathon_b200.worker import ShiftWorker
+
+    # the link's own bandwidth: one 1 GiB pinned -> device copy, best of 3
+    src = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    best = None
+    for _ in range(3):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        best = ms if best is None else min(best, ms)
+    link = (1 << 30) / (best / 1e3) / 1e9
+    del src, dst
+
+    store = ShiftStore(budget_tokens=sum(cfg.history), device="cpu")
+    for si, per_layer in enumerate(wl.stores):
+        bufs = {}
+        for n, t in zip(names, per_layer, strict=True):
+            h = store._alloc(t.shape, t.dtype, "cpu")
+            h.copy_(t)
+            bufs[n] = h
+        store.adopt(f"s{si}", bufs, 0, cfg.history[si])
+    worker = ShiftWorker(store, cfg.block_size, wl.inv_freq.cpu(), layout=args.layout, fp8=fp8,
+                         k_scales=wl.k_scales)
+    worker.register(dict(zip(names, wl.kv, strict=True)))
+    for _ in range(3):
+        worker.load(jobs)
+    steps = 5
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        worker.load(jobs, check=True)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    staged = worker.mover.last_staged_bytes
+    return {
+        "value": round(turn_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 3),
+        "api": "marathon_b200.worker.ShiftWorker.load (store on device='cpu', pinned)",
+        "staged_bytes_per_step": staged, "chunks": worker.mover.last_chunks,
+        "copies": worker.mover.last_copies,
+        "link_achieved": round(staged / (ms / 1e3) / 1e9, 2),
+        "link_peak": round(link, 2), "link_frac": round(staged / (ms / 1e3) / 1e9 / link, 4),
+        "link_peak_kind": "measured live: one 1 GiB pinned host->device copy",
+        "steps": steps,
+    }
+
+
 def native_arm(args) -> None:
     import torch.distributed as dist
 
@@ -411,6 +474,10 @@ def native_arm(args) -> None:
                "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": 4, "api": "marathon_b200.worker.ShiftWorker.load"}
 
+    host_tier = None
+    if world == 1 and not args.no_host_tier and not args.no_e2e:
+        host_tier = host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device)
+
     peak, peak_kind = peaks()
     achieved = rank_bytes / (kernel_ms / 1e3) / 1e9
     units = cfg.shifted_tokens * cfg.layers  # (token, layer) units of the whole turn
@@ -464,6 +531,7 @@ def native_arm(args) -> None:
             },
             "e2e": e2e,
             "save": save,
+            "host_tier": host_tier,
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,

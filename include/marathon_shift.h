@@ -214,6 +214,32 @@ MSHIFT_API int mshift_load_noalloc(const mshift_paged* paged, int32_t rotary,
 /* Most distinct deltas one mshift_load_noalloc call accepts. */
 MSHIFT_API int32_t mshift_noalloc_max_deltas(void);
 
+/*
+ * Store tier off the GPU: staged copies.  A store whose buffers live in
+ * pinned host memory or on another GPU is never read by a kernel; its rows
+ * are copied (copy engines, one cudaMemcpyAsync per range, in array order,
+ * cudaMemcpyDefault) into a device staging buffer that mshift_load reads, and
+ * mshift_save's staging rows are copied back the same way.  `copies` is a
+ * host array; ranges of zero bytes are skipped.  Host ranges must be pinned
+ * for the copy to be asynchronous.  No counterpart in the reference: its
+ * store is device-only (docs/protocol.md:49, src/marathon/shift_store.py:251-253).
+ */
+typedef struct mshift_copy {
+  void* dst;
+  const void* src;
+  int64_t bytes;
+} mshift_copy;
+
+MSHIFT_API int mshift_stage(const mshift_copy* copies, int32_t n, void* stream);
+
+/*
+ * Enable direct (NVLink) copies from `peer_device` to the current device, for
+ * a store tier on another GPU.  MSHIFT_OK if enabled or already enabled,
+ * MSHIFT_EUNSUPPORTED if the pair has no peer access.  Kernels never
+ * dereference peer memory: only mshift_stage copies read it.
+ */
+MSHIFT_API int mshift_enable_peer(int32_t peer_device);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,8 @@ EXPORTS = (
     "mshift_load_noalloc",
     "mshift_noalloc_max_deltas",
     "mshift_set_load_kernel",
+    "mshift_stage",
+    "mshift_enable_peer",
 )
 
 
@@ -88,6 +90,9 @@ RUN_DTYPE = np.dtype(
 )
 assert RUN_DTYPE.itemsize == ctypes.sizeof(Run) == 56
 
+#: ``mshift_copy``: one staged range (dst, src, bytes)
+COPY_DTYPE = np.dtype([("dst", "<u8"), ("src", "<u8"), ("bytes", "<i8")])
+
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
@@ -121,6 +126,8 @@ _SIGNATURES = {
     ),
     "mshift_noalloc_max_deltas": (_I32, []),
     "mshift_set_load_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "mshift_stage": (ctypes.c_int, [_P, _I32, _P]),
+    "mshift_enable_peer": (ctypes.c_int, [_I32]),
 }
 
 _lock = threading.Lock()

@@ -1211,6 +1211,41 @@ const char* mshift_strerror(int status) {
 
 const char* mshift_last_cuda_error(void) { return g_cuda_error; }
 
+int mshift_stage(const mshift_copy* copies, int32_t n, void* stream) {
+  if (n < 0 || (n > 0 && copies == nullptr)) return MSHIFT_EINVAL;
+  for (int32_t i = 0; i < n; ++i) {
+    const mshift_copy& c = copies[i];
+    if (c.bytes < 0 || (c.bytes > 0 && (c.dst == nullptr || c.src == nullptr)))
+      return MSHIFT_EINVAL;
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  for (int32_t i = 0; i < n; ++i) {
+    const mshift_copy& c = copies[i];
+    if (c.bytes == 0) continue;
+    cudaError_t e = cudaMemcpyAsync(c.dst, c.src, static_cast<size_t>(c.bytes),
+                                    cudaMemcpyDefault, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return MSHIFT_OK;
+}
+
+int mshift_enable_peer(int32_t peer_device) {
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (peer_device == cur) return MSHIFT_OK;
+  int ok = 0;
+  e = cudaDeviceCanAccessPeer(&ok, cur, peer_device);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (!ok) return MSHIFT_EUNSUPPORTED;
+  e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();  // drop the recorded "already enabled" status
+    return MSHIFT_OK;
+  }
+  return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
+}
+
 }  // extern "C"
 
 // ============================================ allocation-free batched load

@@ -356,6 +356,11 @@ class _Staging:
         ev.record(stream)
         self.done[slot] = ev
 
+    def copy_err(self, slot: int, dst: torch.Tensor, stream) -> None:
+        """Queue a copy of the slot's error word into ``dst`` (pinned int32 [1]) on ``stream``."""
+        with torch.cuda.stream(stream):
+            dst.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
+
     def read_err(self, slot: int, stream) -> int:
         self.err_host.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
         stream.synchronize()
@@ -608,8 +613,11 @@ class Launcher:
         inv_freq: torch.Tensor,
         *,
         k_scales: torch.Tensor | None = None,
+        first_layer: int = 0,
+        n_layers: int | None = None,
     ) -> Prepared:
         _require_cuda(inv_freq, "inv_freq")
+        n_layers = self._layer_range(first_layer, n_layers)
         deltas = sorted({int(r.delta) for r in runs if int(r.delta) != 0})
         if self.geo.dtype == _lib.E4M3 and deltas:
             if k_scales is None:
@@ -617,7 +625,7 @@ class Launcher:
             k_scales = k_scales.to(device=self.device, dtype=torch.float32).contiguous()
             if k_scales.numel() < len(self.layers):
                 raise ShiftError("need one K scale per layer")
-        p = self._prepare("load", runs, store, deltas, 0, len(self.layers))
+        p = self._prepare("load", runs, store, deltas, first_layer, n_layers)
         p.inv_freq = inv_freq if inv_freq.dtype == torch.float32 else inv_freq.float()
         p.k_scales = k_scales if deltas else None
         if deltas:
@@ -634,10 +642,14 @@ class Launcher:
         self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
         n_layers: int | None = None,
     ) -> Prepared:
+        n_layers = self._layer_range(first_layer, n_layers)
+        return self._prepare("save", runs, store, [], first_layer, n_layers)
+
+    def _layer_range(self, first_layer: int, n_layers: int | None) -> int:
         n_layers = len(self.layers) - first_layer if n_layers is None else int(n_layers)
         if first_layer < 0 or n_layers <= 0 or first_layer + n_layers > len(self.layers):
             raise ShiftError(f"layer range [{first_layer}, +{n_layers}) outside the caches")
-        return self._prepare("save", runs, store, [], first_layer, n_layers)
+        return n_layers
 
     def launch(self, p: Prepared, *, tables: bool = True, main: bool = True) -> int:
         """Issue the native launches of a prepared batch; returns how many were issued."""
@@ -653,14 +665,16 @@ class Launcher:
                 )
                 n += 1
             if main:
+                off = 8 * p.first_layer
                 _lib.check(
                     self.lib.mshift_load(
                         ctypes.byref(self.paged), 2 * half, p.runs, p.n_runs, p.tile_tokens,
                         p.tiles, p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
-                        self.layers.k_ptrs.data_ptr(), self.layers.v_ptrs.data_ptr(),
+                        self.layers.k_ptrs.data_ptr() + off, self.layers.v_ptrs.data_ptr() + off,
                         p.tables.data_ptr() if p.tables is not None else None, p.n_deltas,
-                        p.k_scales.data_ptr() if p.k_scales is not None else None, p.base,
-                        stream,
+                        p.k_scales.data_ptr() + 4 * p.first_layer
+                        if p.k_scales is not None else None,
+                        p.base, stream,
                     ),
                     "mshift_load",
                 )

@@ -148,7 +148,7 @@ class ShiftStore:
         keep = entry.filled
         self._version += 1
         for name, old in list(entry.layers.items()):
-            fresh = torch.zeros((new_cap, *old.shape[1:]), dtype=old.dtype, device=old.device)
+            fresh = self._alloc((new_cap, *old.shape[1:]), old.dtype, old.device)
             n = min(keep, old.shape[0])
             fresh[:n] = old[:n]
             entry.layers[name] = fresh
@@ -202,7 +202,9 @@ class ShiftStore:
         if entry is None or dst_start + n > entry.capacity or not self.allocate:
             return
         buf = self._buffer(entry, layer, src.shape[1:], src.dtype)
-        buf[dst_start : dst_start + n] = src.to(buf.device, non_blocking=True)
+        # a host-tier buffer is written synchronously: it may be regrown (a CPU
+        # copy) before the stream would have finished a non-blocking write
+        buf[dst_start : dst_start + n] = src.to(buf.device, non_blocking=buf.is_cuda)
         self.saved_token_layers += n
 
     def read(self, session: str, layer: str, start: int, n: int) -> torch.Tensor | None:
@@ -243,10 +245,17 @@ class ShiftStore:
             return None
         return entry
 
+    def _alloc(self, shape, dtype, device) -> torch.Tensor:
+        """A zeroed buffer; on the host tier (``device="cpu"``) pinned when CUDA is up,
+        so the staged copies to and from the GPU run on the copy engines."""
+        if torch.device(device).type == "cpu" and torch.cuda.is_available():
+            return torch.zeros(shape, dtype=dtype, pin_memory=True)
+        return torch.zeros(shape, dtype=dtype, device=device)
+
     def _buffer(self, entry: _Entry, layer: str, row_shape, dtype) -> torch.Tensor:
         buf = entry.layers.get(layer)
         if buf is None:
-            buf = torch.zeros((entry.capacity, *row_shape), dtype=dtype, device=self.device)
+            buf = self._alloc((entry.capacity, *row_shape), dtype, self.device)
             entry.layers[layer] = buf
             self._version += 1
         return buf

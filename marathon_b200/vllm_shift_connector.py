@@ -60,6 +60,7 @@ from .shift_store import (
     plan_save,
     slots,
 )
+from .store_tier import DEFAULT_CHUNK_BYTES
 from .worker import LoadJob, SaveJob, ShiftWorker
 
 if TYPE_CHECKING:
@@ -183,7 +184,11 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         self._rotary = rotary
         cache_dtype = str(getattr(vllm_config.cache_config, "cache_dtype", "auto"))
         self._fp8 = cache_dtype.startswith("fp8")
-        self._worker = ShiftWorker(self._store, self._bs, self._inv_freq, fp8=self._fp8)
+        # a store_device other than this worker's GPU ("cpu": pinned host memory) is
+        # reached through staged copies of this many bytes per chunk
+        chunk = int(extra.get("stage_chunk_bytes", DEFAULT_CHUNK_BYTES))
+        self._worker = ShiftWorker(self._store, self._bs, self._inv_freq, fp8=self._fp8,
+                                   chunk_bytes=chunk)
         self._kv: dict[str, torch.Tensor] = {}
         self._hnd: bool | None = None
         self._head_size: int | None = None
@@ -412,6 +417,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             row = self._store.read(job.session, name, job.src_start, job.length)
             if row is None:
                 continue
+            row = row.to(kv.device)  # a host or peer store tier
             sh = self._shift(job.delta, kv.device)
             kf = row[..., :d].float()
             h = d // 2

@@ -23,6 +23,7 @@ import torch
 from .paged import KVLayers
 from .shift_kernels import Launcher, RunSpec, ShiftError
 from .shift_store import ShiftStore, slots as host_slots
+from .store_tier import DEFAULT_CHUNK_BYTES, StagedMover, is_staged
 
 logger = logging.getLogger("vllm.marathon_shift")
 
@@ -81,6 +82,7 @@ class ShiftWorker:
         layout: str | None = None,
         fp8: bool = False,
         k_scales: torch.Tensor | None = None,
+        chunk_bytes: int = DEFAULT_CHUNK_BYTES,
     ) -> None:
         self.store = store
         self.block_size = int(block_size)
@@ -91,6 +93,9 @@ class ShiftWorker:
         self.layers: KVLayers | None = None
         self.launcher: Launcher | None = None
         self.inv: torch.Tensor | None = None
+        # a store in host memory or on another GPU is reached by staged copies
+        self.chunk_bytes = int(chunk_bytes)
+        self.mover: StagedMover | None = None
 
     @property
     def registered(self) -> bool:
@@ -100,6 +105,11 @@ class ShiftWorker:
         self.layers = KVLayers(kv_caches, self.block_size, self.layout, fp8=self.fp8)
         self.launcher = Launcher(self.layers)
         self.inv = self.inv_cpu.to(self.layers.device)
+        if is_staged(self.store.device, self.layers.device):
+            self.mover = StagedMover(self.launcher, self.chunk_bytes)
+            peer = torch.device(self.store.device)
+            if peer.type == "cuda":
+                self.mover.enable_peer(peer.index)
         if self.k_scales is not None:
             self.k_scales = self.k_scales.to(self.layers.device, torch.float32)
         return self.layers
@@ -137,7 +147,8 @@ class ShiftWorker:
             runs.append(_run(row, job.src_start, job.length, job.delta, job.block_ids, job.slots,
                              job.dst_start, tables))
         view = self.store.view(list(rows), names)
-        self.launcher.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
+        mover = self.mover or self.launcher
+        mover.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
         return accepted
 
     # ---------------------------------------------------------------- save
@@ -175,7 +186,8 @@ class ShiftWorker:
         if not runs:
             return 0
         view = self.store.view(list(rows), names)
-        self.launcher.save(runs, view, first_layer=first, n_layers=len(names), check=check)
+        mover = self.mover or self.launcher
+        mover.save(runs, view, first_layer=first, n_layers=len(names), check=check)
         done = sum(r.length for r in runs)
         self.store.mark_saved(done, len(names))
         return done * len(names)
