@@ -152,31 +152,65 @@ struct E4m3 {
   }
 };
 
-// e4m3 codes of r[k] / s (four values, one 32-bit word), each exactly the
-// saturating round-to-nearest-even of the correctly rounded quotient
-// __fdiv_rn(r, s).  q = r * (1/s) is within 2.5 ulp of that quotient.
-// Converting q*(1-2^-21) and q*(1+2^-21) (at least 3.5 ulp on each side of q)
-// gives the same codes for both ends exactly when every value in between, the
-// quotient included, rounds to those codes (the conversion is monotonic).
-// Only when some end differs -- a value sits next to an e4m3 rounding
-// boundary -- are the quotients formed by division; the test is voted across
-// the warp so that rare path is taken by whole warps.
+// e4m3 requantisation: the code of r / s must be exactly the saturating
+// round-to-nearest-even of the correctly rounded quotient __fdiv_rn(r, s).
+// With inv = 1/s rounded, idn = inv*(1-2^-21) and iup = inv*(1+2^-21) (both
+// rounded), r*idn and r*iup lie more than 4 ulp below and above the quotient
+// (three roundings of 2^-24 against a 2^-21 offset).  Converting both ends
+// gives the same code exactly when every value in between -- the rounded
+// quotient included -- rounds to that code (the conversion is monotonic).
+// Where the two ends differ (a value next to an e4m3 rounding boundary), the
+// quotient is formed by division.
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float2 v) {
   return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3));
 }
 
-__device__ __forceinline__ uint32_t requant4(const float2* r, float s, float inv) {
-  const float2 i2 = make_float2(inv, inv);
-  const float2 dn = make_float2(0.99999952316284180f, 0.99999952316284180f);  // 1 - 2^-21
-  const float2 up = make_float2(1.00000047683715820f, 1.00000047683715820f);  // 1 + 2^-21
-  const float2 q0 = __fmul2_rn(r[0], i2), q1 = __fmul2_rn(r[1], i2);
-  const uint32_t lo = cvt_e4m3x2(__fmul2_rn(q0, dn)) | (cvt_e4m3x2(__fmul2_rn(q1, dn)) << 16);
-  const uint32_t hi = cvt_e4m3x2(__fmul2_rn(q0, up)) | (cvt_e4m3x2(__fmul2_rn(q1, up)) << 16);
-  if (!__any_sync(__activemask(), lo != hi)) return lo;
-  if (lo == hi) return lo;
+// Codes of the four values r[0..1] (one 32-bit word) from the low end; ORs
+// the low-end / high-end difference into `miss`.
+__device__ __forceinline__ uint32_t requant4(const float2* r, float2 idn, float2 iup,
+                                             uint32_t& miss) {
+  const uint32_t lo = cvt_e4m3x2(__fmul2_rn(r[0], idn)) | (cvt_e4m3x2(__fmul2_rn(r[1], idn)) << 16);
+  const uint32_t hi = cvt_e4m3x2(__fmul2_rn(r[0], iup)) | (cvt_e4m3x2(__fmul2_rn(r[1], iup)) << 16);
+  miss |= lo ^ hi;
+  return lo;
+}
+
+__device__ __forceinline__ uint32_t requant4_div(const float2* r, float s) {
   const float2 e0 = make_float2(__fdiv_rn(r[0].x, s), __fdiv_rn(r[0].y, s));
   const float2 e1 = make_float2(__fdiv_rn(r[1].x, s), __fdiv_rn(r[1].y, s));
   return cvt_e4m3x2(e0) | (cvt_e4m3x2(e1) << 16);
+}
+
+// Dequantise and rotate one word pair of e4m3 codes: ra = x*c - y*s and
+// rb = y*c + x*s with x, y = code * scale, every product rounded on its own
+// (packed multiplies; the sums are scalar so no multiply is fused into them).
+__device__ __forceinline__ void rotate_word_e4m3(uint32_t aw, uint32_t bw, const float* cs,
+                                                 const float* sn, float scale, float2* ra,
+                                                 float2* rb) {
+  float x[4], y[4];
+  E4m3::unpack(aw, x);
+  E4m3::unpack(bw, y);
+  const float4 c4 = *reinterpret_cast<const float4*>(cs);
+  const float4 s4 = *reinterpret_cast<const float4*>(sn);
+  const float2 sc = make_float2(scale, scale);
+  const float2 c01 = make_float2(c4.x, c4.y), c23 = make_float2(c4.z, c4.w);
+  const float2 s01 = make_float2(s4.x, s4.y), s23 = make_float2(s4.z, s4.w);
+  const float2 x01 = __fmul2_rn(make_float2(x[0], x[1]), sc);
+  const float2 x23 = __fmul2_rn(make_float2(x[2], x[3]), sc);
+  const float2 y01 = __fmul2_rn(make_float2(y[0], y[1]), sc);
+  const float2 y23 = __fmul2_rn(make_float2(y[2], y[3]), sc);
+  {
+    const float2 xc = __fmul2_rn(x01, c01), ys = __fmul2_rn(y01, s01);
+    const float2 yc = __fmul2_rn(y01, c01), xs = __fmul2_rn(x01, s01);
+    ra[0] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+    rb[0] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+  }
+  {
+    const float2 xc = __fmul2_rn(x23, c23), ys = __fmul2_rn(y23, s23);
+    const float2 yc = __fmul2_rn(y23, c23), xs = __fmul2_rn(x23, s23);
+    ra[1] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+    rb[1] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+  }
 }
 
 // Rotate one pair of partner vectors in place: `a` holds elements
@@ -184,72 +218,63 @@ __device__ __forceinline__ uint32_t requant4(const float2* r, float s, float inv
 // Works one 32-bit word (kPer elements) at a time to keep few values live; the
 // products of two elements share one packed fp32x2 multiply (each lane rounds
 // on its own), the sums are scalar, so the results are those of the scalar
-// __fmul_rn / __fsub_rn / __fadd_rn sequence.
+// __fmul_rn / __fsub_rn / __fadd_rn sequence.  For e4m3, each word is
+// requantised from the two interval ends; a word whose ends disagree is
+// requantised by division instead.
 template <class E>
 __device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, const float* sn,
                                             float scale, float inv_scale) {
-  constexpr int P = E::kPer;
+  if constexpr (E::kScaled) {
+    const float dn = __fmul_rn(inv_scale, 0.99999952316284180f);  // inv * (1 - 2^-21)
+    const float up = __fmul_rn(inv_scale, 1.00000047683715820f);  // inv * (1 + 2^-21)
+    const float2 idn = make_float2(dn, dn), iup = make_float2(up, up);
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    float x[P], y[P];
-    E::unpack(a.w[w], x);
-    E::unpack(b.w[w], y);
-    if constexpr (E::kScaled) {
-      // e4m3: four elements per word; cos/sin as float4; one requantisation
-      // test per word, taken warp-uniformly
-      const float4 c4 = *reinterpret_cast<const float4*>(cs + 4 * w);
-      const float4 s4 = *reinterpret_cast<const float4*>(sn + 4 * w);
-      const float2 sc = make_float2(scale, scale);
-      const float2 c01 = make_float2(c4.x, c4.y), c23 = make_float2(c4.z, c4.w);
-      const float2 s01 = make_float2(s4.x, s4.y), s23 = make_float2(s4.z, s4.w);
-      const float2 x01 = __fmul2_rn(make_float2(x[0], x[1]), sc);
-      const float2 x23 = __fmul2_rn(make_float2(x[2], x[3]), sc);
-      const float2 y01 = __fmul2_rn(make_float2(y[0], y[1]), sc);
-      const float2 y23 = __fmul2_rn(make_float2(y[2], y[3]), sc);
+    for (int w = 0; w < 4; ++w) {
       float2 ra[2], rb[2];
-      {
-        const float2 xc = __fmul2_rn(x01, c01), ys = __fmul2_rn(y01, s01);
-        const float2 yc = __fmul2_rn(y01, c01), xs = __fmul2_rn(x01, s01);
-        ra[0] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
-        rb[0] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-      }
-      {
-        const float2 xc = __fmul2_rn(x23, c23), ys = __fmul2_rn(y23, s23);
-        const float2 yc = __fmul2_rn(y23, c23), xs = __fmul2_rn(x23, s23);
-        ra[1] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
-        rb[1] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-      }
-      a.w[w] = requant4(ra, scale, inv_scale);
-      b.w[w] = requant4(rb, scale, inv_scale);
-      continue;
-    } else if constexpr (P == 1) {
-      const float c = cs[w], s = sn[w];
-      float xe = x[0], ye = y[0];
-      if constexpr (E::kScaled) {
-        xe = __fmul_rn(xe, scale);
-        ye = __fmul_rn(ye, scale);
-      }
-      x[0] = __fsub_rn(__fmul_rn(xe, c), __fmul_rn(ye, s));
-      y[0] = __fadd_rn(__fmul_rn(ye, c), __fmul_rn(xe, s));
-    } else {
-#pragma unroll
-      for (int j = 0; j < P / 2; ++j) {
-        const float2 c = *reinterpret_cast<const float2*>(cs + P * w + 2 * j);
-        const float2 s = *reinterpret_cast<const float2*>(sn + P * w + 2 * j);
-        const float2 x2 = make_float2(x[2 * j], x[2 * j + 1]);
-        const float2 y2 = make_float2(y[2 * j], y[2 * j + 1]);
-        // packed products, scalar adds: __fadd_rn / __fsub_rn are never merged
-        // with a multiply, so every product is rounded before it is added
-        const float2 xc = __fmul2_rn(x2, c), ys = __fmul2_rn(y2, s);
-        const float2 yc = __fmul2_rn(y2, c), xs = __fmul2_rn(x2, s);
-        const float2 ra = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
-        const float2 rb = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-        x[2 * j] = ra.x, x[2 * j + 1] = ra.y;
-        y[2 * j] = rb.x, y[2 * j + 1] = rb.y;
+      rotate_word_e4m3(a.w[w], b.w[w], cs + 4 * w, sn + 4 * w, scale, ra, rb);
+      uint32_t m = 0;
+      const uint32_t la = requant4(ra, idn, iup, m);
+      const uint32_t lb = requant4(rb, idn, iup, m);
+      if (m != 0u) {  // rare: an end sits across an e4m3 rounding boundary
+        a.w[w] = requant4_div(ra, scale);
+        b.w[w] = requant4_div(rb, scale);
+      } else {
+        a.w[w] = la;
+        b.w[w] = lb;
       }
     }
-    a.w[w] = E::pack(x);
-    b.w[w] = E::pack(y);
+  } else {
+    constexpr int P = E::kPer;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      float x[P], y[P];
+      E::unpack(a.w[w], x);
+      E::unpack(b.w[w], y);
+      if constexpr (P == 1) {
+        const float c = cs[w], s = sn[w];
+        const float xe = x[0], ye = y[0];
+        x[0] = __fsub_rn(__fmul_rn(xe, c), __fmul_rn(ye, s));
+        y[0] = __fadd_rn(__fmul_rn(ye, c), __fmul_rn(xe, s));
+      } else {
+#pragma unroll
+        for (int j = 0; j < P / 2; ++j) {
+          const float2 c = *reinterpret_cast<const float2*>(cs + P * w + 2 * j);
+          const float2 s = *reinterpret_cast<const float2*>(sn + P * w + 2 * j);
+          const float2 x2 = make_float2(x[2 * j], x[2 * j + 1]);
+          const float2 y2 = make_float2(y[2 * j], y[2 * j + 1]);
+          // packed products, scalar adds: __fadd_rn / __fsub_rn are never merged
+          // with a multiply, so every product is rounded before it is added
+          const float2 xc = __fmul2_rn(x2, c), ys = __fmul2_rn(y2, s);
+          const float2 yc = __fmul2_rn(y2, c), xs = __fmul2_rn(x2, s);
+          const float2 ra = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
+          const float2 rb = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
+          x[2 * j] = ra.x, x[2 * j + 1] = ra.y;
+          y[2 * j] = rb.x, y[2 * j + 1] = rb.y;
+        }
+      }
+      a.w[w] = E::pack(x);
+      b.w[w] = E::pack(y);
+    }
   }
 }
 
