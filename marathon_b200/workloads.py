@@ -120,6 +120,9 @@ def c4_config(seed: int = 4, sessions: int = 64) -> Config:
 CONFIGS: dict[str, Config] = {
     "c0": Config("c0", "Qwen3-0.6B", 28, (4096,), ((Segment(1024, 1061, 3072),),),
                  free_blocks=(300,)),
+    # c0 with the prefix moved too, as a delta-0 segment (a plain paged copy)
+    "c0z": Config("c0z", "Qwen3-0.6B", 28, (4096,),
+                  ((Segment(0, 0, 1024), Segment(1024, 1061, 3072)),), free_blocks=(300,)),
     "c1": Config("c1", "Qwen3-8B", 36, (16384,), (_c1_segments(),)),
     "c2": Config("c2", "Qwen3-14B", 40, (30720,), ((Segment(2112, 2292, 28608),),)),
     "c3": Config("c3", "Qwen3-14B", 40, (30720,), ((Segment(2112, 2292, 28608),),),

@@ -348,7 +348,7 @@ def _torch_reference_rows(store_rows: torch.Tensor, table: torch.Tensor) -> torc
     return torch.cat((out.to(store_rows.dtype), store_rows[..., d:]), dim=-1)
 
 
-@pytest.mark.parametrize("name", ["c0", "c1", "c2"])
+@pytest.mark.parametrize("name", ["c0", "c0z", "c1", "c2"])
 def test_baseline_configs_full_size_vs_torch_fp32(cuda, load_kernel, name):
     """Every layer of configs c0-c2 at full size, against torch fp32 on the same GPU."""
     from marathon_b200.workloads import build, config
