@@ -312,30 +312,39 @@ class _Staging:
     A batch's descriptors — run records, store pointer table, capacities,
     deltas, host block tables and a zeroed error word — reach the device in
     ONE host-to-device copy.  Two slots alternate so the next batch can be
-    packed while the previous batch's kernels still read theirs.
+    packed while the previous batch's kernels still read theirs.  The copies
+    go through ``mshift_stage`` (one ``cudaMemcpyAsync`` each) with records
+    prepared once per slot.
     """
 
-    def __init__(self, device: torch.device) -> None:
+    def __init__(self, device: torch.device, lib) -> None:
         self.device = device
+        self.lib = lib
         self.cap = 0
         self.host: list[torch.Tensor] = []
         self.dev: list[torch.Tensor] = []
-        self.done: list[torch.cuda.Event | None] = [None, None]
+        self.done = [torch.cuda.Event(), torch.cuda.Event()]
+        self.used = [False, False]
         self.slot = 0
         self.err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        # per slot: [upload record, error-word read-back record]
+        self.rec = np.zeros((2, 2), dtype=_lib.COPY_DTYPE)
+        self.rec_addr = self.rec.ctypes.data
 
     def _ensure(self, n: int) -> None:
         if n <= self.cap:
             return
-        for ev in self.done:
-            if ev is not None:
-                ev.synchronize()
+        for k in range(2):
+            if self.used[k]:
+                self.done[k].synchronize()
         cap = 1 << max(12, (n - 1).bit_length())
         self.host = [torch.empty(cap, dtype=torch.uint8).pin_memory() for _ in range(2)]
         self.host_np = [h.numpy() for h in self.host]
         self.dev = [torch.empty(cap, dtype=torch.uint8, device=self.device) for _ in range(2)]
         self.dev_ptr = [d.data_ptr() for d in self.dev]
-        self.done = [None, None]
+        for k in range(2):
+            self.rec[k, 0] = (self.dev_ptr[k], self.host[k].data_ptr(), 0)
+            self.rec[k, 1] = (self.err_host.data_ptr(), self.dev_ptr[k], 4)
         self.cap = cap
 
     def begin(self, n: int) -> tuple[int, np.ndarray, int]:
@@ -343,18 +352,18 @@ class _Staging:
         self._ensure(n)
         slot = self.slot
         self.slot ^= 1
-        ev = self.done[slot]
-        if ev is not None:
-            ev.synchronize()
+        if self.used[slot]:
+            self.done[slot].synchronize()
         return slot, self.host_np[slot], self.dev_ptr[slot]
 
-    def upload(self, slot: int, n: int) -> None:
-        self.dev[slot][:n].copy_(self.host[slot][:n], non_blocking=True)
+    def upload(self, slot: int, n: int, stream_ptr: int) -> None:
+        self.rec[slot, 0]["bytes"] = n
+        _lib.check(self.lib.mshift_stage(self.rec_addr + slot * 2 * _lib.COPY_DTYPE.itemsize, 1,
+                                         stream_ptr), "mshift_stage (descriptors)")
 
     def finish(self, slot: int, stream) -> None:
-        ev = torch.cuda.Event()
-        ev.record(stream)
-        self.done[slot] = ev
+        self.done[slot].record(stream)
+        self.used[slot] = True
 
     def copy_err(self, slot: int, dst: torch.Tensor, stream) -> None:
         """Queue a copy of the slot's error word into ``dst`` (pinned int32 [1]) on ``stream``."""
@@ -362,7 +371,8 @@ class _Staging:
             dst.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
 
     def read_err(self, slot: int, stream) -> int:
-        self.err_host.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
+        rec = self.rec_addr + (slot * 2 + 1) * _lib.COPY_DTYPE.itemsize
+        _lib.check(self.lib.mshift_stage(rec, 1, stream.cuda_stream), "mshift_stage (status)")
         stream.synchronize()
         return int(self.err_host[0])
 
@@ -391,6 +401,7 @@ class Prepared:
     tables: torch.Tensor | None = None
     k_scales: torch.Tensor | None = None
     inv_freq: torch.Tensor | None = None
+    stream: object = None  # the torch stream current when the batch was prepared
 
 
 class Launcher:
@@ -414,7 +425,8 @@ class Launcher:
         self.paged = self.geo.struct()
         props = torch.cuda.get_device_properties(self.device)
         self._grid = props.multi_processor_count * self.CTAS_PER_SM
-        self.staging = _Staging(self.device)
+        self.staging = _Staging(self.device, self.lib)
+        self._tiles: dict = {}
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
         self._tables: list[torch.Tensor | None] = [None, None]
@@ -435,6 +447,16 @@ class Launcher:
         tile count just under a multiple of the resident CTAs instead of a
         last wave that leaves most of them idle.
         """
+        key = (n_layers, tokens if lengths is None else tuple(lengths))
+        hit = self._tiles.get(key)
+        if hit is not None:
+            return hit
+        if len(self._tiles) > 4096:
+            self._tiles.clear()
+        self._tiles[key] = tt = self._tile_search(tokens, n_layers, lengths)
+        return tt
+
+    def _tile_search(self, tokens: int, n_layers: int, lengths) -> int:
         heads = self.geo.heads
         t_max = max(1, int(self.lib.mshift_default_tile_tokens(heads)))
         t_min = max(1, t_max // 2)
@@ -448,9 +470,9 @@ class Launcher:
     _RUN = struct.Struct("<qqQQiiiiii")  # mshift_run, 56 bytes
     _SMALL = 32  # batches up to this many runs are packed record by record
 
-    def _prepare(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
+    def _prepare(self, kind, runs, store, deltas, first_layer, n_layers, stream) -> Prepared:
         if len(runs) <= self._SMALL:
-            return self._prepare_small(kind, runs, store, deltas, first_layer, n_layers)
+            return self._prepare_small(kind, runs, store, deltas, first_layer, n_layers, stream)
         n_runs = len(runs)
         S, L = store.ptrs.shape
         if L != n_layers:
@@ -530,13 +552,13 @@ class Launcher:
             )
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total)
+        self.staging.upload(slot, total, stream.cuda_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
-                        base + o_deltas, len(deltas), total, tt)
+                        base + o_deltas, len(deltas), total, tt, stream=stream)
 
-    def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers) -> Prepared:
+    def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers, stream) -> Prepared:
         """``_prepare`` for a few runs: records packed straight into the pinned slot."""
         n_runs = len(runs)
         S, L = store.ptrs.shape
@@ -600,11 +622,11 @@ class Launcher:
             struct.pack_into("<q", host, o_deltas + 8 * k, d)
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total)
+        self.staging.upload(slot, total, stream.cuda_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
-                        base + o_deltas, len(deltas), total, tt)
+                        base + o_deltas, len(deltas), total, tt, stream=stream)
 
     def prepare_load(
         self,
@@ -625,7 +647,8 @@ class Launcher:
             k_scales = k_scales.to(device=self.device, dtype=torch.float32).contiguous()
             if k_scales.numel() < len(self.layers):
                 raise ShiftError("need one K scale per layer")
-        p = self._prepare("load", runs, store, deltas, first_layer, n_layers)
+        p = self._prepare("load", runs, store, deltas, first_layer, n_layers,
+                          torch.cuda.current_stream(self.device))
         p.inv_freq = inv_freq if inv_freq.dtype == torch.float32 else inv_freq.float()
         p.k_scales = k_scales if deltas else None
         if deltas:
@@ -643,7 +666,8 @@ class Launcher:
         n_layers: int | None = None,
     ) -> Prepared:
         n_layers = self._layer_range(first_layer, n_layers)
-        return self._prepare("save", runs, store, [], first_layer, n_layers)
+        return self._prepare("save", runs, store, [], first_layer, n_layers,
+                             torch.cuda.current_stream(self.device))
 
     def _layer_range(self, first_layer: int, n_layers: int | None) -> int:
         n_layers = len(self.layers) - first_layer if n_layers is None else int(n_layers)
@@ -653,7 +677,7 @@ class Launcher:
 
     def launch(self, p: Prepared, *, tables: bool = True, main: bool = True) -> int:
         """Issue the native launches of a prepared batch; returns how many were issued."""
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        stream = p.stream.cuda_stream
         n = 0
         if p.kind == "load":
             half = int(p.inv_freq.numel())
@@ -696,7 +720,7 @@ class Launcher:
         return n
 
     def finish(self, p: Prepared, check: bool) -> None:
-        stream = torch.cuda.current_stream(self.device)
+        stream = p.stream
         self.staging.finish(p.slot, stream)
         if check:
             _raise_bits(self.staging.read_err(p.slot, stream), f"shift {p.kind}")
