@@ -348,6 +348,34 @@ def _torch_reference_rows(store_rows: torch.Tensor, table: torch.Tensor) -> torc
     return torch.cat((out.to(store_rows.dtype), store_rows[..., d:]), dim=-1)
 
 
+def _paged_rows(kv: torch.Tensor, layout: str, blk: torch.Tensor, off: torch.Tensor):
+    """``[n, heads, 2D]`` rows of one layer's paged cache at (block, offset) pairs."""
+    if layout == "nhd":
+        return kv[blk, off]
+    if layout == "hnd":
+        return kv[blk, :, off]
+    if layout == "split":
+        return torch.cat((kv[0][blk, off], kv[1][blk, off]), dim=-1)
+    return torch.cat((kv[blk, 0, off], kv[blk, 1, off]), dim=-1)  # split_blocks
+
+
+def _check_workload_vs_torch(wl, layout: str, tag) -> None:
+    """Every run x layer of a loaded workload against torch fp32 on the same GPU."""
+    cfg = wl.cfg
+    deltas = sorted({r.delta for r in wl.runs if r.delta})
+    tables = sk.rope_tables(torch.tensor(deltas, device=wl.kv[0].device), wl.inv_freq)
+    for li in range(cfg.layers):
+        for r in wl.runs:
+            rows = wl.stores[r.session][li][r.store_start : r.store_start + r.length]
+            want = _torch_reference_rows(rows, tables[deltas.index(r.delta)]) if r.delta else rows
+            bt = wl.block_tables[r.session].long()
+            pos = torch.arange(r.paged_start, r.paged_start + r.length, device=rows.device)
+            blk = bt[pos // cfg.block_size]
+            off = pos % cfg.block_size
+            got = _paged_rows(wl.kv[li], layout, blk, off)
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (tag, li, r)
+
+
 @pytest.mark.parametrize("name", ["c0", "c0z", "c1", "c2"])
 def test_baseline_configs_full_size_vs_torch_fp32(cuda, load_kernel, name):
     """Every layer of configs c0-c2 at full size, against torch fp32 on the same GPU."""
@@ -358,18 +386,39 @@ def test_baseline_configs_full_size_vs_torch_fp32(cuda, load_kernel, name):
     launcher = Launcher(KVLayers(wl.kv, cfg.block_size, "nhd"))
     launcher.load(wl.runs, wl.store_view(), wl.inv_freq, check=True)
     torch.cuda.synchronize()
-    deltas = sorted({r.delta for r in wl.runs if r.delta})
-    tables = sk.rope_tables(torch.tensor(deltas, device=cuda), wl.inv_freq)
-    for li in range(cfg.layers):
-        for r in wl.runs:
-            rows = wl.stores[r.session][li][r.store_start : r.store_start + r.length]
-            want = _torch_reference_rows(rows, tables[deltas.index(r.delta)]) if r.delta else rows
-            bt = wl.block_tables[r.session].long()
-            pos = torch.arange(r.paged_start, r.paged_start + r.length, device=cuda)
-            blk = bt[pos // cfg.block_size]
-            off = pos % cfg.block_size
-            got = wl.kv[li][blk, off]
-            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (name, li)
+    _check_workload_vs_torch(wl, "nhd", name)
+    del wl
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("layout", ["hnd", "split", "split_blocks"])
+def test_c1_full_segments_other_layouts_vs_torch_fp32(cuda, load_kernel, layout):
+    """c1's three full-length segments (2 of 36 layers) in the non-default layouts."""
+    from marathon_b200.workloads import build, config, scaled
+
+    cfg = scaled(config("c1"), layers=2)
+    wl = build(cfg, cuda, layout=layout)
+    launcher = Launcher(KVLayers(wl.kv, cfg.block_size, layout))
+    launcher.load(wl.runs, wl.store_view(), wl.inv_freq, check=True)
+    torch.cuda.synchronize()
+    _check_workload_vs_torch(wl, layout, layout)
+    del wl
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("lo,hi", [(3, 4), (4, 8)])
+def test_c4_sessions_head_shard_vs_torch_fp32(cuda, load_kernel, lo, hi):
+    """c4's 64 sessions (2 of 36 layers) as one tensor-parallel rank sees them:
+    heads [lo, hi) of 8, every session's segments in one launch."""
+    from marathon_b200.workloads import build, config, scaled
+
+    cfg = scaled(config("c4"), layers=2)
+    wl = build(cfg, cuda, head_lo=lo, head_hi=hi)
+    launcher = Launcher(KVLayers(wl.kv, cfg.block_size, "nhd"))
+    launcher.load(wl.runs, wl.store_view(), wl.inv_freq, check=True)
+    torch.cuda.synchronize()
+    assert len(wl.runs) > 64
+    _check_workload_vs_torch(wl, "nhd", (lo, hi))
     del wl
     torch.cuda.empty_cache()
 
