@@ -307,51 +307,52 @@ def _align(n: int, a: int = 16) -> int:
 
 
 class _Staging:
-    """Pinned host + device staging of one batch's descriptors, double-buffered.
+    """Pinned host + device staging of one batch's descriptors, a ring of slots.
 
     A batch's descriptors — run records, store pointer table, capacities,
     deltas, host block tables and a zeroed error word — reach the device in
-    ONE host-to-device copy.  Two slots alternate so the next batch can be
-    packed while the previous batch's kernels still read theirs.  The copies
+    ONE host-to-device copy.  Slots rotate (two by default) so the next batch
+    can be packed while earlier batches' kernels still read theirs.  The copies
     go through ``mshift_stage`` (one ``cudaMemcpyAsync`` each) with records
     prepared once per slot.
     """
 
-    def __init__(self, device: torch.device, lib) -> None:
+    def __init__(self, device: torch.device, lib, slots: int = 2) -> None:
         self.device = device
         self.lib = lib
+        self.n = int(slots)
         self.cap = 0
         self.host: list[torch.Tensor] = []
         self.dev: list[torch.Tensor] = []
-        self.done = [torch.cuda.Event(), torch.cuda.Event()]
-        self.used = [False, False]
+        self.done = [torch.cuda.Event() for _ in range(self.n)]
+        self.used = [False] * self.n
         self.slot = 0
         self.err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         # per slot: [upload record, error-word read-back record]
-        self.rec = np.zeros((2, 2), dtype=_lib.COPY_DTYPE)
+        self.rec = np.zeros((self.n, 2), dtype=_lib.COPY_DTYPE)
         self.rec_addr = self.rec.ctypes.data
 
     def _ensure(self, n: int) -> None:
         if n <= self.cap:
             return
-        for k in range(2):
+        for k in range(self.n):
             if self.used[k]:
                 self.done[k].synchronize()
         cap = 1 << max(12, (n - 1).bit_length())
-        self.host = [torch.empty(cap, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.host = [torch.empty(cap, dtype=torch.uint8).pin_memory() for _ in range(self.n)]
         self.host_np = [h.numpy() for h in self.host]
-        self.dev = [torch.empty(cap, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        self.dev = [torch.empty(cap, dtype=torch.uint8, device=self.device) for _ in range(self.n)]
         self.dev_ptr = [d.data_ptr() for d in self.dev]
-        for k in range(2):
+        for k in range(self.n):
             self.rec[k, 0] = (self.dev_ptr[k], self.host[k].data_ptr(), 0)
             self.rec[k, 1] = (self.err_host.data_ptr(), self.dev_ptr[k], 4)
         self.cap = cap
 
     def begin(self, n: int) -> tuple[int, np.ndarray, int]:
-        """Pick a free slot: (slot, host bytes view, device base address)."""
+        """Pick the next slot, waiting for its previous batch: (slot, host view, device base)."""
         self._ensure(n)
         slot = self.slot
-        self.slot ^= 1
+        self.slot = (slot + 1) % self.n
         if self.used[slot]:
             self.done[slot].synchronize()
         return slot, self.host_np[slot], self.dev_ptr[slot]
@@ -413,7 +414,8 @@ class Launcher:
     check (one 4-byte D2H read and a stream sync).
     """
 
-    def __init__(self, layers: KVLayers, tile_tokens: int | None = None) -> None:
+    def __init__(self, layers: KVLayers, tile_tokens: int | None = None,
+                 staging_slots: int = 2) -> None:
         if layers.k_ptrs is None:
             raise ShiftError("the batched kernels need CUDA caches")
         self.layers = layers
@@ -425,11 +427,11 @@ class Launcher:
         self.paged = self.geo.struct()
         props = torch.cuda.get_device_properties(self.device)
         self._grid = props.multi_processor_count * self.CTAS_PER_SM
-        self.staging = _Staging(self.device, self.lib)
+        self.staging = _Staging(self.device, self.lib, staging_slots)
         self._tiles: dict = {}
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
-        self._tables: list[torch.Tensor | None] = [None, None]
+        self._tables: list[torch.Tensor | None] = [None] * staging_slots
 
     #: resident CTAs of the load/save kernel per SM (register-limited, B200)
     CTAS_PER_SM = 2

@@ -127,16 +127,48 @@ def is_staged(store_device_name: str, cache_device: torch.device) -> bool:
     return d.index is not None and d.index != cache_device.index
 
 
+@dataclass
+class StagedLoad:
+    """A staged load in flight: one completion event per cache layer.
+
+    ``wait_layer(i)`` makes a stream wait until layer ``i``'s rows are in the
+    paged cache (vLLM's ``wait_for_layer_load``); ``check()`` waits for the
+    whole load on the host and raises on any rejected token.
+    """
+
+    layer_done: list
+    last: torch.cuda.Event
+    errs: torch.Tensor
+    n_chunks: int
+
+    def wait_layer(self, layer: int, stream=None) -> None:
+        (stream or torch.cuda.current_stream()).wait_event(self.layer_done[layer])
+
+    def wait_all(self, stream=None) -> None:
+        (stream or torch.cuda.current_stream()).wait_event(self.last)
+
+    def check(self) -> None:
+        self.last.synchronize()
+        bits = int(np.bitwise_or.reduce(self.errs[: self.n_chunks].numpy()))
+        if bits:
+            raise ShiftError(f"staged shift load: {_lib.describe_bits(bits)} (error bits {bits:#x})")
+
+
 class StagedMover:
     """Batched load/save between an off-GPU store and the paged caches, through staging."""
 
+    #: descriptor slots of the mover's own launcher: enough that issuing a whole
+    #: load's chunks rarely waits on the host for an earlier chunk's kernel
+    DESCRIPTOR_SLOTS = 64
+
     def __init__(self, launcher: Launcher, chunk_bytes: int = DEFAULT_CHUNK_BYTES) -> None:
-        self.launcher = launcher
+        self.launcher = Launcher(launcher.layers, staging_slots=self.DESCRIPTOR_SLOTS)
         self.device = launcher.device
         self.lib = launcher.lib
         self.chunk_bytes = int(chunk_bytes)
         self.row_bytes_per_elem = _ELEM_BYTES[launcher.geo.dtype]
         self.copy_stream = torch.cuda.Stream(self.device)
+        self.load_stream = torch.cuda.Stream(self.device)  # kernels of asynchronous loads
         self._slots: list[torch.Tensor | None] = [None, None]
         self._freed: list[torch.cuda.Event | None] = [None, None]
         self._peers: set[int] = set()
@@ -236,42 +268,67 @@ class StagedMover:
     # --------------------------------------------------------------- load
     def load(self, runs: list[RunSpec], store: StoreView, inv_freq: torch.Tensor, *,
              k_scales: torch.Tensor | None = None, check: bool = True) -> None:
-        """Every run x every layer from the off-GPU store into the paged caches."""
+        """Every run x every layer from the off-GPU store into the paged caches,
+        ordered on the current stream."""
         if not runs:
             return
+        job = self._load(runs, store, inv_freq, k_scales, torch.cuda.current_stream(self.device))
+        if check:
+            job.check()
+
+    def load_async(self, runs: list[RunSpec], store: StoreView, inv_freq: torch.Tensor, *,
+                   k_scales: torch.Tensor | None = None) -> StagedLoad | None:
+        """The same load on the mover's own streams, returning at once.
+
+        It starts after the work already queued on the current stream; layer
+        ``i`` is in place once ``StagedLoad.wait_layer(i)``'s event fires, so a
+        forward pass can run layer ``i`` while later layers are still crossing
+        the host link.  Errors surface in ``StagedLoad.check()``.
+        """
+        if not runs:
+            return None
+        self.load_stream.wait_stream(torch.cuda.current_stream(self.device))
+        return self._load(runs, store, inv_freq, k_scales, self.load_stream)
+
+    def _load(self, runs, store, inv_freq, k_scales, compute) -> StagedLoad:
         n_layers = len(self.launcher.layers)
         self._check_runs(runs, store, n_layers)
         row_bytes = self._row_bytes(store)
         chunks = plan_chunks([r.length for r in runs], row_bytes, n_layers, self.chunk_bytes)
         size = max(c.nbytes for c in chunks)
-        compute = torch.cuda.current_stream(self.device)
         errs = self._err_buffer(len(chunks))
+        layer_done: list = [None] * n_layers
         copies = 0
-        for ci, ch in enumerate(chunks):
-            k = ci % 2
-            base = self._slot(k, size)
-            rec = self._copies(ch, runs, store, row_bytes, base, to_slot=True)
-            if self._freed[k] is not None:
-                self.copy_stream.wait_event(self._freed[k])  # its last reader is done
-            self._stage(rec, self.copy_stream)
-            copies += len(rec)
-            staged = torch.cuda.Event()
-            staged.record(self.copy_stream)
-            compute.wait_event(staged)
-            view = self._slot_view(ch, base, store)
-            p = self.launcher.prepare_load(self._piece_runs(ch, runs), view, inv_freq,
-                                           k_scales=k_scales, first_layer=ch.first_layer,
-                                           n_layers=ch.n_layers)
-            self.launcher.launch(p)
-            self.launcher.staging.copy_err(p.slot, errs[ci : ci + 1], compute)
-            self.launcher.finish(p, False)
-            freed = torch.cuda.Event()
-            freed.record(compute)
-            self._freed[k] = freed
+        # the copy stream must not overtake earlier work on the compute stream
+        # (a save whose rows this load reads back, a cache the caller filled)
+        self.copy_stream.wait_stream(compute)
+        with torch.cuda.stream(compute):
+            for ci, ch in enumerate(chunks):
+                k = ci % 2
+                base = self._slot(k, size)
+                rec = self._copies(ch, runs, store, row_bytes, base, to_slot=True)
+                if self._freed[k] is not None:
+                    self.copy_stream.wait_event(self._freed[k])  # its last reader is done
+                self._stage(rec, self.copy_stream)
+                copies += len(rec)
+                staged = torch.cuda.Event()
+                staged.record(self.copy_stream)
+                compute.wait_event(staged)
+                view = self._slot_view(ch, base, store)
+                p = self.launcher.prepare_load(self._piece_runs(ch, runs), view, inv_freq,
+                                               k_scales=k_scales, first_layer=ch.first_layer,
+                                               n_layers=ch.n_layers)
+                self.launcher.launch(p)
+                self.launcher.staging.copy_err(p.slot, errs[ci : ci + 1], compute)
+                self.launcher.finish(p, False)
+                freed = torch.cuda.Event()
+                freed.record(compute)
+                self._freed[k] = freed
+                for layer in range(ch.first_layer, ch.first_layer + ch.n_layers):
+                    layer_done[layer] = freed  # the layer's last chunk so far
         self.last_chunks, self.last_copies = len(chunks), copies
         self.last_staged_bytes = sum(c.nbytes for c in chunks)
-        if check:
-            self._raise(compute, errs, len(chunks), "staged shift load")
+        return StagedLoad(layer_done, freed, errs, len(chunks))
 
     # --------------------------------------------------------------- save
     def save(self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
@@ -291,7 +348,7 @@ class StagedMover:
             k = ci % 2
             base = self._slot(k, size)
             if self._freed[k] is not None:
-                compute.wait_event(self._freed[k])  # the slot's last copy-out is done
+                compute.wait_event(self._freed[k])  # the slot's last user is done
             view = self._slot_view(ch, base, store)
             p = self.launcher.prepare_save(self._piece_runs(ch, runs), view,
                                            first_layer=first_layer + ch.first_layer,

@@ -27,6 +27,12 @@ What changes is the worker side:
   With ``kv_connector_extra_config["batch_save"]`` (or
   ``MARATHON_BATCH_SAVE=1``) the per-layer saves are deferred to
   ``wait_for_save`` and run as one launch over all layers.
+* ``store_device`` other than this worker's GPU (``"cpu"``: pinned host
+  memory, or another GPU) keeps the store off the GPU; loads are staged
+  through a device ring and, unless ``async_tier_load`` is false, run on
+  their own streams while the forward pass proceeds: ``wait_for_layer_load``
+  orders each layer's attention after its rows, ``wait_for_save`` checks the
+  load's status.
 
 Paged layouts: the fused 4-D layouts the reference asserts (NHD/HND,
 ``:393-402``) and the 5-D split layouts of vLLM 0.22's FlashAttention
@@ -167,6 +173,8 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                                  session_cap=cap)
         _STORES.append(self._store)
         self._batch_save = bool(extra.get("batch_save", BATCH_SAVE))
+        # loads from a store off the GPU overlap the forward pass, layer by layer
+        self._async_tier = bool(extra.get("async_tier_load", True))
 
         # scheduler side
         self._table = SessionTable()
@@ -387,8 +395,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                 self._worker.k_scales = self._worker.k_scales.to(self._worker.layers.device)
         jobs = [LoadJob(ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length,
                         block_ids=ld.block_ids) for ld in meta.loads]
+        # a store off the GPU streams in layer by layer behind the forward pass
+        # (wait_for_layer_load orders each layer's attention after its rows);
+        # a device store loads synchronously, as the reference did
+        staged = self._worker.mover is not None and self._async_tier and not VERIFY_LOAD
         t0 = time.perf_counter()
-        done = self._worker.load(jobs, check=True)  # synchronises on the status word
+        done = self._worker.load(jobs, check=True, asynchronous=staged)
         ms = (time.perf_counter() - t0) * 1e3
         geo = self._worker.layers.geometry
         moved = sum(j.length for j in done) * len(self._worker.layers) * geo.heads * \
@@ -397,8 +409,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             logger.info("shift: session %s loaded %d tokens x %d layers from store[%d:%d], "
                         "delta=%d", j.session, j.length, len(self._worker.layers), j.src_start,
                         j.src_start + j.length, j.delta)
-        logger.info("shift: %d load(s) in one launch, copy_ms=%.2f (%.2f MB, %.1f GB/s)",
-                    len(done), ms, moved / 2**20, moved / 2**30 / max(ms / 1e3, 1e-9))
+        if staged:
+            logger.info("shift: %d load(s) queued from the %s store tier (%.2f MB, %.2f ms "
+                        "to queue)", len(done), self._store.device, moved / 2**20, ms)
+        else:
+            logger.info("shift: %d load(s) in one launch, copy_ms=%.2f (%.2f MB, %.1f GB/s)",
+                        len(done), ms, moved / 2**20, moved / 2**30 / max(ms / 1e3, 1e-9))
         if VERIFY_LOAD:
             for j in done:
                 self._verify(j)
@@ -437,7 +453,8 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                         float(diff.max() / want.abs().max().clamp_min(1e-6)))
 
     def wait_for_layer_load(self, layer_name: str) -> None:
-        return
+        if self._worker.pending is not None and layer_name in self._worker.layers.index:
+            self._worker.wait_layer(layer_name)
 
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata, **kw):
         meta = self._get_connector_metadata()
@@ -468,6 +485,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._worker.save(jobs, names, check=False)
 
     def wait_for_save(self):
+        self._worker.finish_pending()  # an asynchronous staged load of this step
         if not self._pending_saves:
             return
         meta = self._get_connector_metadata() if self.has_connector_metadata() else None

@@ -23,7 +23,7 @@ import torch
 from .paged import KVLayers
 from .shift_kernels import Launcher, RunSpec, ShiftError
 from .shift_store import ShiftStore, slots as host_slots
-from .store_tier import DEFAULT_CHUNK_BYTES, StagedMover, is_staged
+from .store_tier import DEFAULT_CHUNK_BYTES, StagedLoad, StagedMover, is_staged
 
 logger = logging.getLogger("vllm.marathon_shift")
 
@@ -96,6 +96,7 @@ class ShiftWorker:
         # a store in host memory or on another GPU is reached by staged copies
         self.chunk_bytes = int(chunk_bytes)
         self.mover: StagedMover | None = None
+        self.pending: StagedLoad | None = None  # an asynchronous staged load in flight
 
     @property
     def registered(self) -> bool:
@@ -115,18 +116,25 @@ class ShiftWorker:
         return self.layers
 
     # ---------------------------------------------------------------- load
-    def load(self, jobs: list[LoadJob], *, check: bool = True) -> list[LoadJob]:
+    def load(self, jobs: list[LoadJob], *, check: bool = True,
+             asynchronous: bool = False) -> list[LoadJob]:
         """Every job x every layer in one launch.  Returns the jobs that were issued.
 
         A job whose rows are not all held (evicted, truncated, a layer never
         saved) stops the batch there, as the reference's load loop returned on
         the first missing layer (``vllm_shift_connector.py:506-513``): jobs
         before it are loaded, it and later ones are not.
+
+        ``asynchronous`` (a store off the GPU only): the staged load runs on
+        its own streams and this returns once it is queued; ``wait_layer``
+        orders a layer's consumers after its rows, ``finish_pending`` checks
+        the outcome.  On a device store the load is synchronous regardless.
         """
         if not jobs:
             return []
         if self.launcher is None:
             raise ShiftError("no KV caches registered")
+        self.finish_pending()
         names = self.layers.names
         accepted: list[LoadJob] = []
         for job in jobs:
@@ -147,9 +155,25 @@ class ShiftWorker:
             runs.append(_run(row, job.src_start, job.length, job.delta, job.block_ids, job.slots,
                              job.dst_start, tables))
         view = self.store.view(list(rows), names)
+        if self.mover is not None and asynchronous:
+            self.pending = self.mover.load_async(runs, view, self.inv, k_scales=self.k_scales)
+            return accepted
         mover = self.mover or self.launcher
         mover.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
         return accepted
+
+    def wait_layer(self, name: str) -> None:
+        """Order the current stream after layer ``name`` of a pending staged load."""
+        if self.pending is not None:
+            self.pending.wait_layer(self.layers.index[name])
+
+    def finish_pending(self) -> None:
+        """Complete a pending staged load: the current stream waits for all of it,
+        the host checks its status (raises :class:`ShiftError` on rejected tokens)."""
+        job, self.pending = self.pending, None
+        if job is not None:
+            job.wait_all()
+            job.check()
 
     # ---------------------------------------------------------------- save
     def save(self, jobs: list[SaveJob], layer_names: list[str] | None = None, *,
@@ -164,6 +188,9 @@ class ShiftWorker:
             return 0
         if self.launcher is None:
             raise ShiftError("no KV caches registered")
+        if self.pending is not None:
+            # the saved rows may be ones the pending load is still writing
+            self.pending.wait_all()
         names = layer_names if layer_names is not None else self.layers.names
         idx = [self.layers.index[n] for n in names]
         first = idx[0]

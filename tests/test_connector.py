@@ -165,13 +165,22 @@ def _oracle_slots(blocks, lo, hi):
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape_kind", ["split", "nhd", "hnd"])
 @pytest.mark.parametrize("batch_save", [False, True])
-def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, batch_save):
-    """Save a prompt layer by layer, then serve an edit turn's load: oracle-exact."""
+@pytest.mark.parametrize("store_device", ["cuda", "cpu"])
+def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, batch_save,
+                                                              store_device):
+    """Save a prompt layer by layer, then serve an edit turn's load: oracle-exact.
+
+    With ``store_device="cpu"`` the store is pinned host memory: saves copy out
+    through staging, and the load streams in asynchronously, each layer
+    awaited through ``wait_for_layer_load`` as the forward pass would.
+    """
     from oracle import shift_oracle as O
 
     H, D, L, NBLK = 8, 128, 4, 96
     conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192,
-                                                 "batch_save": batch_save}),
+                                                 "batch_save": batch_save,
+                                                 "store_device": store_device,
+                                                 "stage_chunk_bytes": 300 * H * 2 * D * 2}),
                                     KVConnectorRole.WORKER, None)
     g = torch.Generator().manual_seed(7)
     shapes = {"split": (2, NBLK, BS, H, D), "nhd": (NBLK, BS, H, 2 * D),
@@ -192,6 +201,7 @@ def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, b
     conn.clear_connector_metadata()
     torch.cuda.synchronize()
     entry = conn._store._sessions["s"]
+    assert all(t.device.type == store_device for t in entry.layers.values())
     saved = {n: entry.layers[n][:600].clone() for n in caches}
     snap = {n: kv.clone() for n, kv in caches.items()}
 
@@ -200,6 +210,12 @@ def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, b
     meta = C.ShiftConnectorMetadata(loads=[C._Load("s", 64, 37, 101, 528, blocks1, BS)])
     conn.bind_connector_metadata(meta)
     conn.start_load_kv(SimpleNamespace(no_compile_layers={}, virtual_engine=0))
+    if store_device == "cpu":
+        assert conn._worker.pending is not None
+        for name in caches:
+            conn.wait_for_layer_load(name)
+        conn.wait_for_save()
+        assert conn._worker.pending is None
     conn.clear_connector_metadata()
     torch.cuda.synchronize()
 

@@ -247,3 +247,35 @@ def test_peer_gpu_store_tier(cuda):
     torch.cuda.synchronize()
     for a, b in zip(host_kv, dev_kv, strict=True):
         assert np.array_equal(_bits(a), _bits(b))
+
+
+@pytest.mark.gpu
+def test_host_tier_async_load_layer_by_layer(cuda):
+    """An asynchronous staged load, consumed layer by layer on the current stream
+    (as a forward pass would), lands the same bits as the device store."""
+    host_w, host_kv, _, jobs, _ = _case(cuda, "cpu", layers=4, chunk_bytes=200 * ROW, seed=13)
+    dev_w, dev_kv, _, djobs, _ = _case(cuda, str(cuda), layers=4, seed=13)
+    dev_w.load(djobs)
+    assert len(host_w.load(jobs, asynchronous=True)) == len(jobs)
+    assert host_w.pending is not None and host_w.mover.last_chunks > 4
+    snaps = []
+    for name, t in zip(host_w.layers.names, host_kv, strict=True):
+        host_w.wait_layer(name)
+        snaps.append(t.clone())  # ordered after exactly this layer's rows
+    host_w.finish_pending()
+    assert host_w.pending is None
+    torch.cuda.synchronize()
+    for a, b in zip(snaps, dev_kv, strict=True):
+        assert np.array_equal(_bits(a), _bits(b))
+
+
+@pytest.mark.gpu
+def test_host_tier_async_load_reports_bad_slots_at_finish(cuda):
+    worker, _, _, jobs, _ = _case(cuda, "cpu", chunk_bytes=64 * ROW, seed=5)
+    bad = jobs[2].slots.clone()
+    bad[0] = -1
+    jobs[2].slots = bad
+    worker.load(jobs, asynchronous=True)
+    with pytest.raises(ShiftError, match="slot outside"):
+        worker.finish_pending()
+    assert worker.pending is None
