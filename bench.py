@@ -308,9 +308,24 @@ def host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device) -> dic
         first.append(time.perf_counter() - t0)
         worker.finish_pending()
         whole.append(time.perf_counter() - t0)
+    # the save direction: the same rows out of the paged caches into host memory
+    from marathon_b200.worker import SaveJob
+
+    saves = [SaveJob(j.session, j.src_start, j.length, block_ids=j.block_ids) for j in jobs]
+    worker.save(saves)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        worker.save(saves, check=True)
+    b.record()
+    torch.cuda.synchronize()
+    save_ms = a.elapsed_time(b) / steps
+    save_staged = worker.mover.last_staged_bytes
     return {
         "value": round(turn_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 3),
         "api": "marathon_b200.worker.ShiftWorker.load (store on device='cpu', pinned)",
+        "save_ms_per_step": round(save_ms, 3),
+        "save_link_achieved": round(save_staged / (save_ms / 1e3) / 1e9, 2),
         "staged_bytes_per_step": staged, "chunks": worker.mover.last_chunks,
         "copies": worker.mover.last_copies,
         "link_achieved": round(staged / (ms / 1e3) / 1e9, 2),
