@@ -472,9 +472,11 @@ class Launcher:
     _RUN = struct.Struct("<qqQQiiiiii")  # mshift_run, 56 bytes
     _SMALL = 32  # batches up to this many runs are packed record by record
 
-    def _prepare(self, kind, runs, store, deltas, first_layer, n_layers, stream) -> Prepared:
+    def _prepare(self, kind, runs, store, deltas, first_layer, n_layers, stream,
+                 upload_stream=None) -> Prepared:
         if len(runs) <= self._SMALL:
-            return self._prepare_small(kind, runs, store, deltas, first_layer, n_layers, stream)
+            return self._prepare_small(kind, runs, store, deltas, first_layer, n_layers, stream,
+                                       upload_stream)
         n_runs = len(runs)
         S, L = store.ptrs.shape
         if L != n_layers:
@@ -554,13 +556,14 @@ class Launcher:
             )
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total, stream.cuda_stream)
+        self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
                         base + o_deltas, len(deltas), total, tt, stream=stream)
 
-    def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers, stream) -> Prepared:
+    def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers, stream,
+                       upload_stream=None) -> Prepared:
         """``_prepare`` for a few runs: records packed straight into the pinned slot."""
         n_runs = len(runs)
         S, L = store.ptrs.shape
@@ -624,7 +627,7 @@ class Launcher:
             struct.pack_into("<q", host, o_deltas + 8 * k, d)
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total, stream.cuda_stream)
+        self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
@@ -639,7 +642,13 @@ class Launcher:
         k_scales: torch.Tensor | None = None,
         first_layer: int = 0,
         n_layers: int | None = None,
+        upload_stream=None,
     ) -> Prepared:
+        """Pack a load batch and queue its descriptor copy.
+
+        The copy goes on the current stream, or on ``upload_stream`` when the
+        caller orders it itself (it must complete before the batch's launch).
+        """
         _require_cuda(inv_freq, "inv_freq")
         n_layers = self._layer_range(first_layer, n_layers)
         deltas = sorted({int(r.delta) for r in runs if int(r.delta) != 0})
@@ -650,7 +659,7 @@ class Launcher:
             if k_scales.numel() < len(self.layers):
                 raise ShiftError("need one K scale per layer")
         p = self._prepare("load", runs, store, deltas, first_layer, n_layers,
-                          torch.cuda.current_stream(self.device))
+                          torch.cuda.current_stream(self.device), upload_stream)
         p.inv_freq = inv_freq if inv_freq.dtype == torch.float32 else inv_freq.float()
         p.k_scales = k_scales if deltas else None
         if deltas:

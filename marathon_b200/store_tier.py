@@ -82,9 +82,12 @@ def plan_chunks(lengths: list[int], row_bytes: int, n_layers: int,
         per = max(1, chunk_bytes // per_layer)
         pieces = [Piece(i, 0, n) for i, n in enumerate(lengths)]
         offsets = np.concatenate(([0], np.cumsum(lengths[:-1]))).astype(np.int64) * row_bytes
+        # the first chunk is one layer: a consumer waiting for layer 0 waits
+        # for one layer's transfer, not a whole chunk's
+        starts = [0] + list(range(1, n_layers, per)) if per > 1 else list(range(n_layers))
         return [
-            Chunk(l0, min(per, n_layers - l0), pieces, offsets.tolist(), per_layer)
-            for l0 in range(0, n_layers, per)
+            Chunk(l0, min(per if l0 else 1, n_layers - l0), pieces, offsets.tolist(), per_layer)
+            for l0 in starts
         ]
     groups: list[list[Piece]] = []
     cur: list[Piece] = []
@@ -307,6 +310,14 @@ class StagedMover:
                 k = ci % 2
                 base = self._slot(k, size)
                 rec = self._copies(ch, runs, store, row_bytes, base, to_slot=True)
+                # the chunk's descriptors ride the copy stream just ahead of its
+                # rows: a descriptor copy queued on the compute stream would wait
+                # in the copy engine behind the next chunk's rows
+                view = self._slot_view(ch, base, store)
+                p = self.launcher.prepare_load(self._piece_runs(ch, runs), view, inv_freq,
+                                               k_scales=k_scales, first_layer=ch.first_layer,
+                                               n_layers=ch.n_layers,
+                                               upload_stream=self.copy_stream)
                 if self._freed[k] is not None:
                     self.copy_stream.wait_event(self._freed[k])  # its last reader is done
                 self._stage(rec, self.copy_stream)
@@ -314,10 +325,6 @@ class StagedMover:
                 staged = torch.cuda.Event()
                 staged.record(self.copy_stream)
                 compute.wait_event(staged)
-                view = self._slot_view(ch, base, store)
-                p = self.launcher.prepare_load(self._piece_runs(ch, runs), view, inv_freq,
-                                               k_scales=k_scales, first_layer=ch.first_layer,
-                                               n_layers=ch.n_layers)
                 self.launcher.launch(p)
                 self.launcher.staging.copy_err(p.slot, errs[ci : ci + 1], compute)
                 self.launcher.finish(p, False)

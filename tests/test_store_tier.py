@@ -48,9 +48,10 @@ def test_plan_chunks_covers_every_row_once_within_the_budget(chunk_rows):
         assert ch.offsets == list(np.cumsum([0] + sizes[:-1]))  # dense, row aligned
         assert ch.layer_bytes == sum(sizes)
         assert all(o % 16 == 0 for o in ch.offsets)
-    if chunk_rows >= sum(lengths):  # whole layers per chunk
+    if chunk_rows >= sum(lengths):  # whole layers per chunk; the first holds one
         per = chunk_rows // sum(lengths)
-        assert len(chunks) == -(-n_layers // per)
+        assert chunks[0].n_layers == 1
+        assert len(chunks) == (1 + -(-(n_layers - 1) // per) if per > 1 else n_layers)
         assert all(len(ch.pieces) == len(lengths) for ch in chunks)
     else:
         assert all(ch.n_layers == 1 for ch in chunks)
