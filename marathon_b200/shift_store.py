@@ -271,14 +271,16 @@ class ShiftStore:
             self._buffer(entry, name, (heads, row), dtype)
         return True
 
-    def loadable(self, session: str, layers: list[str], start: int, n: int) -> str | None:
+    def loadable(self, session: str, layers: list[str], start: int, n: int,
+                 layer_set: frozenset | None = None) -> str | None:
         """First layer whose rows ``[start, start + n)`` cannot be read, or None.
 
         The batched load checks a whole load before launching, where the
-        reference's per-layer ``read`` discovered a gap mid-loop.
+        reference's per-layer ``read`` discovered a gap mid-loop.  ``layer_set``
+        is ``layers`` as a set, for callers that check many loads.
         """
         entry = self._readable(session, start, n)
-        if entry is not None and entry.layers.keys() >= set(layers):
+        if entry is not None and entry.layers.keys() >= (layer_set or set(layers)):
             return None
         for name in layers:
             if entry is None or name not in entry.layers:

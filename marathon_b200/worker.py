@@ -104,6 +104,7 @@ class ShiftWorker:
 
     def register(self, kv_caches: dict[str, torch.Tensor]) -> KVLayers:
         self.layers = KVLayers(kv_caches, self.block_size, self.layout, fp8=self.fp8)
+        self._name_set = frozenset(self.layers.names)
         self.launcher = Launcher(self.layers)
         self.inv = self.inv_cpu.to(self.layers.device)
         if is_staged(self.store.device, self.layers.device):
@@ -136,9 +137,11 @@ class ShiftWorker:
             raise ShiftError("no KV caches registered")
         self.finish_pending()
         names = self.layers.names
+        name_set = self._name_set
         accepted: list[LoadJob] = []
         for job in jobs:
-            missing = self.store.loadable(job.session, names, job.src_start, job.length)
+            missing = self.store.loadable(job.session, names, job.src_start, job.length,
+                                          name_set)
             if missing is not None:
                 logger.error("shift: session %s has no stored KV for %s; load skipped",
                              job.session, missing)
