@@ -278,7 +278,7 @@ def host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device) -> dic
     for si, per_layer in enumerate(wl.stores):
         bufs = {}
         for n, t in zip(names, per_layer, strict=True):
-            h = store._alloc(t.shape, t.dtype, "cpu")
+            h = store.new_buffer(t.shape, t.dtype, "cpu")
             h.copy_(t)
             bufs[n] = h
         store.adopt(f"s{si}", bufs, 0, cfg.history[si])

@@ -660,7 +660,7 @@ class Launcher:
         caller orders it itself (it must complete before the batch's launch).
         """
         _require_cuda(inv_freq, "inv_freq")
-        n_layers = self._layer_range(first_layer, n_layers)
+        n_layers = self.layer_range(first_layer, n_layers)
         deltas = sorted({int(r.delta) for r in runs if int(r.delta) != 0})
         if self.geo.dtype == _lib.E4M3 and deltas:
             if k_scales is None:
@@ -686,11 +686,13 @@ class Launcher:
         self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
         n_layers: int | None = None,
     ) -> Prepared:
-        n_layers = self._layer_range(first_layer, n_layers)
+        n_layers = self.layer_range(first_layer, n_layers)
         return self._prepare("save", runs, store, [], first_layer, n_layers,
                              torch.cuda.current_stream(self.device))
 
-    def _layer_range(self, first_layer: int, n_layers: int | None) -> int:
+    def layer_range(self, first_layer: int, n_layers: int | None) -> int:
+        """Layers of a batch starting at ``first_layer`` (default: to the last); raises
+        if the range leaves the registered caches."""
         n_layers = len(self.layers) - first_layer if n_layers is None else int(n_layers)
         if first_layer < 0 or n_layers <= 0 or first_layer + n_layers > len(self.layers):
             raise ShiftError(f"layer range [{first_layer}, +{n_layers}) outside the caches")

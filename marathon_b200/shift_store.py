@@ -148,7 +148,7 @@ class ShiftStore:
         keep = entry.filled
         self._version += 1
         for name, old in list(entry.layers.items()):
-            fresh = self._alloc((new_cap, *old.shape[1:]), old.dtype, old.device)
+            fresh = self.new_buffer((new_cap, *old.shape[1:]), old.dtype, old.device)
             n = min(keep, old.shape[0])
             fresh[:n] = old[:n]
             entry.layers[name] = fresh
@@ -245,7 +245,7 @@ class ShiftStore:
             return None
         return entry
 
-    def _alloc(self, shape, dtype, device) -> torch.Tensor:
+    def new_buffer(self, shape, dtype, device) -> torch.Tensor:
         """A zeroed buffer; on the host tier (``device="cpu"``) pinned when CUDA is up,
         so the staged copies to and from the GPU run on the copy engines."""
         if torch.device(device).type == "cpu" and torch.cuda.is_available():
@@ -255,7 +255,7 @@ class ShiftStore:
     def _buffer(self, entry: _Entry, layer: str, row_shape, dtype) -> torch.Tensor:
         buf = entry.layers.get(layer)
         if buf is None:
-            buf = self._alloc((entry.capacity, *row_shape), dtype, self.device)
+            buf = self.new_buffer((entry.capacity, *row_shape), dtype, self.device)
             entry.layers[layer] = buf
             self._version += 1
         return buf

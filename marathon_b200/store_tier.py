@@ -343,7 +343,7 @@ class StagedMover:
         """Paged rows of every run x layers ``[first_layer, +n_layers)`` out to the store."""
         if not runs:
             return
-        n_layers = self.launcher._layer_range(first_layer, n_layers)
+        n_layers = self.launcher.layer_range(first_layer, n_layers)
         self._check_runs(runs, store, n_layers)
         row_bytes = self._row_bytes(store)
         chunks = plan_chunks([r.length for r in runs], row_bytes, n_layers, self.chunk_bytes)

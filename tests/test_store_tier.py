@@ -120,7 +120,7 @@ def _case(cuda, store_device, *, fp8=False, layers=3, chunk_bytes=None, seed=0):
     for si, rows in enumerate(host_rows):
         bufs = {}
         for n, t in zip(names, rows, strict=True):
-            b = store._alloc(t.shape, t.dtype, store_device)
+            b = store.new_buffer(t.shape, t.dtype, store_device)
             b.copy_(t)
             bufs[n] = b
         store.adopt(f"s{si}", bufs, 0, caps[si])
