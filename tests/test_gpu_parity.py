@@ -258,6 +258,12 @@ def test_batched_load_head_geometries(cuda, load_kernel, d, rotary):
     _run_batched_load(cuda, "nhd", d=d, rotary=rotary, seed=d + rotary)
 
 
+@pytest.mark.parametrize("dtype,d", [(O.F16, 64), (O.F16, 256), (O.E4M3, 256)])
+def test_batched_load_other_dtype_head_sizes(cuda, load_kernel, dtype, d):
+    """The remaining compiled (dtype, head_size) kernels, full rotary."""
+    _run_batched_load(cuda, "nhd", dtype=dtype, d=d, seed=d + 7)
+
+
 @pytest.mark.parametrize("heads", [1, 2, 4])
 def test_batched_load_head_shards(cuda, load_kernel, heads):
     """The per-rank shapes of head-sharded tensor parallelism (8 heads over 8/4/2 ranks)."""
