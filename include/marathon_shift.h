@@ -127,6 +127,10 @@ MSHIFT_API int mshift_scatter_shifted(const void* src, int64_t src_tok_stride,
  * (k_ptrs[l], v_ptrs[l]) with K rotated by tables[r.table].
  * tiles_per_layer = sum over runs of ceil(len / tile_tokens); each run's
  * tile_begin is the exclusive prefix of that sum (mshift_plan_tiles fills it).
+ * With n_tables > 0 the kernel is launched with programmatic stream
+ * serialization: its CTAs may start while the kernel just before it in the
+ * stream (normally mshift_rope_tables) finishes, and wait for that kernel's
+ * completion before touching memory, so stream order holds as usual.
  * Replaces: the per-layer loop of MarathonShiftConnector.start_load_kv
  * (src/marathon/vllm_shift_connector.py:495-518) = ShiftStore.read
  * (src/marathon/shift_store.py:238-250) + scatter_shifted per layer and load.

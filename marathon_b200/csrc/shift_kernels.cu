@@ -311,11 +311,27 @@ __device__ __forceinline__ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// Programmatic dependent launch.  The batched kernels are launched so that
+// their CTAs may become resident while the preceding kernel in the stream
+// (the rotation-table kernel) is still running; each thread first waits
+// here until that kernel has completed and its writes are visible.  Launched
+// without the attribute (or after a copy) the wait returns at once.
+__device__ __forceinline__ void wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the dependent kernel of the stream start launching its CTAs now; it
+// still reads nothing of ours before this grid has completed.
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // One templated kernel for both directions.
 //   SAVE = false: store rows -> paged cache, K rotated (load)
 //   SAVE = true : paged cache -> store rows, bit copy (save)
 template <class E, int D, int ROT, bool SAVE>
 __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const KArgs a) {
+  wait_prior_grid();
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;      // 16-byte vectors per K (or V) row
@@ -607,6 +623,7 @@ template <class E, int D, int ROT>
 __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_load_kernel(
     const KArgs a, int parts,
                                                                      int part_tokens) {
+  wait_prior_grid();
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;
@@ -855,6 +872,7 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
 // sin are evaluated in double precision and rounded once to fp32.
 __global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float* inv_freq,
                                    int32_t half, float* out) {
+  allow_dependents();  // the load kernel may launch; it waits for our writes
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)n * half) return;
   const int64_t d = i / half;
@@ -969,14 +987,36 @@ bool strides_aligned(int es, std::initializer_list<int64_t> strides) {
   return true;
 }
 
-int launch(KernelFn fn, int slot, const KArgs& args, cudaStream_t stream) {
+// Launch with programmatic stream serialization (see wait_prior_grid).
+template <class... Params, class... Args>
+cudaError_t launch_dependent(void (*fn)(Params...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
+int launch(KernelFn fn, int slot, const KArgs& args, cudaStream_t stream, bool pdl = false) {
   const int64_t total = (int64_t)args.tiles_per_layer * args.n_layers;
   if (total <= 0) return MSHIFT_OK;
   int grid = 0;
   int st = grid_for(fn, slot, total, &grid);
   if (st != MSHIFT_OK) return st;
-  fn<<<grid, kThreads, 0, stream>>>(args);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (pdl) {
+    e = launch_dependent(fn, dim3(grid), dim3(kThreads), 0, stream, args);
+  } else {
+    fn<<<grid, kThreads, 0, stream>>>(args);
+    e = cudaGetLastError();
+  }
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
 }
 
@@ -993,7 +1033,8 @@ std::atomic<int> g_load_kernel{MSHIFT_KERNEL_AUTO};
 
 // Launch the TMA bulk load; returns MSHIFT_EUNSUPPORTED when the geometry does
 // not fit a stage (the caller then uses the 128-bit-load kernel).
-int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStream_t stream) {
+int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStream_t stream,
+                bool pdl) {
   int part = static_cast<int>(v->bulk_stage_bytes / row_bytes);
   if (part > args.tile_tokens) part = args.tile_tokens;
   if (part > kBulkMaxPart) part = kBulkMaxPart;
@@ -1029,8 +1070,12 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
     const int64_t cap = (int64_t)g_grid.sms[dev] * g_grid.bulk_occ[dev][vi];
     grid = static_cast<int>(items < cap ? items : cap);
   }
-  v->bulk<<<grid, kBulkThreads, smem, stream>>>(args, parts, part);
-  e = cudaGetLastError();
+  if (pdl) {
+    e = launch_dependent(v->bulk, dim3(grid), dim3(kBulkThreads), smem, stream, args, parts, part);
+  } else {
+    v->bulk<<<grid, kBulkThreads, smem, stream>>>(args, parts, part);
+    e = cudaGetLastError();
+  }
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
 }
 
@@ -1084,12 +1129,15 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   const int kind = g_load_kernel.load(std::memory_order_relaxed);
   const bool want_bulk =
       kind == MSHIFT_KERNEL_BULK || (kind == MSHIFT_KERNEL_AUTO && paged->dtype == MSHIFT_E4M3);
+  // a load with rotation tables normally follows the table kernel directly:
+  // let its CTAs launch while that kernel finishes (they wait for its writes)
+  const bool pdl = !save && n_tables > 0;
   if (!save && want_bulk && st_head == 2 * paged->head_size && st_tok == row_elems) {
-    const int st = launch_bulk(v, a, row_elems * es, static_cast<cudaStream_t>(stream));
+    const int st = launch_bulk(v, a, row_elems * es, static_cast<cudaStream_t>(stream), pdl);
     if (st != MSHIFT_EUNSUPPORTED) return st;
   }
   return launch(save ? v->save : v->load, variant_slot(v, save), a,
-                static_cast<cudaStream_t>(stream));
+                static_cast<cudaStream_t>(stream), pdl);
 }
 
 }  // namespace mshift
