@@ -8,3 +8,5 @@ Modules mirror the reference package ``marathon`` for this path:
 """
 
 __version__ = "0.1.0"
+
+from . import torch_ops  # noqa: E402,F401  registers torch.ops.marathon.*
