@@ -194,6 +194,10 @@ class StagedMover:
             if self._freed[k] is not None:
                 self._freed[k].synchronize()
             buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=self.device)
+            # used on the mover's own streams: the allocator must not hand the
+            # memory out again while work queued there may still touch it
+            buf.record_stream(self.copy_stream)
+            buf.record_stream(self.load_stream)
             self._slots[k] = buf
         return buf.data_ptr()
 
