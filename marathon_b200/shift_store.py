@@ -31,6 +31,13 @@ SLAB = 2048
 DEFAULT_STORE_TOKENS = 32768
 
 
+def _settle_host_copies(buffers) -> None:
+    """Before a host-tier buffer is copied on the CPU (growth), let the GPU finish
+    the staged copies that may still be writing it."""
+    if torch.cuda.is_available() and any(not b.is_cuda for b in buffers):
+        torch.cuda.synchronize()
+
+
 def slots(block_ids: list[int], lo: int, hi: int, block_size: int) -> torch.Tensor:
     """Flat slot indices of positions ``[lo, hi)`` through a block table (int64, host).
 
@@ -147,6 +154,7 @@ class ShiftStore:
             self.evictions += 1
         keep = entry.filled
         self._version += 1
+        _settle_host_copies(entry.layers.values())
         for name, old in list(entry.layers.items()):
             fresh = self.new_buffer((new_cap, *old.shape[1:]), old.dtype, old.device)
             n = min(keep, old.shape[0])

@@ -66,6 +66,7 @@ from .shift_store import (
     plan_save,
     slots,
 )
+from .extent_store import ExtentStore
 from .store_tier import DEFAULT_CHUNK_BYTES
 from .worker import LoadJob, SaveJob, ShiftWorker
 
@@ -121,6 +122,7 @@ class _Load:
     length: int
     block_ids: list[int]
     block_size: int
+    gen: int = -1  # extent-store mode: the generation whose keys are loaded
 
     @property
     def slots(self) -> torch.Tensor:
@@ -138,6 +140,7 @@ class _Save:
     length: int
     block_ids: list[int]
     block_size: int
+    gen: int = -1  # extent-store mode: the generation computing these keys
 
     @property
     def slots(self) -> torch.Tensor:
@@ -149,6 +152,18 @@ class _Save:
 class ShiftConnectorMetadata(KVConnectorMetadata):
     loads: list[_Load] = field(default_factory=list)
     saves: list[_Save] = field(default_factory=list)
+    # extent-store mode: (session, gen, pos0, n) extents the view no longer uses
+    releases: list[tuple[str, int, int, int]] = field(default_factory=list)
+
+
+class _GenCover:
+    """``covers`` of one generation of an :class:`ExtentStore`, for ``plan_load``."""
+
+    def __init__(self, store: ExtentStore, gen: int) -> None:
+        self.store, self.gen = store, gen
+
+    def covers(self, session: str, start: int, n: int) -> bool:
+        return self.store.locate(session, self.gen, start, n) is not None
 
 
 def _rope_theta(hf) -> float:
@@ -169,8 +184,14 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                                os.environ.get("MARATHON_STORE_TOKENS", DEFAULT_STORE_TOKENS)))
         device = str(extra.get("store_device", "cuda"))
         cap = int(extra.get("session_tokens", 0) or 0)
-        self._store = ShiftStore(budget, device, allocate=(role == KVConnectorRole.WORKER),
-                                 session_cap=cap)
+        # "window": the reference's flat per-session store; "extents": the
+        # generation-tagged interval store (reuse without re-saving)
+        self._extents = str(extra.get("store_mode", "window")) == "extents"
+        if self._extents:
+            self._store = ExtentStore(budget, device, allocate=(role == KVConnectorRole.WORKER))
+        else:
+            self._store = ShiftStore(budget, device, allocate=(role == KVConnectorRole.WORKER),
+                                     session_cap=cap)
         _STORES.append(self._store)
         self._batch_save = bool(extra.get("batch_save", BATCH_SAVE))
         # loads from a store off the GPU overlap the forward pass, layer by layer
@@ -179,7 +200,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         # scheduler side
         self._table = SessionTable()
         self._params: dict[str, dict[str, Any]] = {}
-        self._plans: dict[str, tuple[int, int, int]] = {}
+        self._plans: dict[str, tuple[int, int, int, int]] = {}
         self._multi: dict[str, list[dict]] = {}
         self._need_load: set[str] = set()
         self._blocks: dict[str, list[int]] = {}
@@ -231,11 +252,18 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             hi = min(int(ld["dst_end"]), limit) // self._bs * self._bs
             if hi - lo < self._bs:
                 continue
-            if not self._store.covers(session, lo - delta, hi - lo):
+            if not self._cover(ld).covers(session, lo - delta, hi - lo):
                 logger.warning("shift: gapfill dropping [%d,%d): store lost the source", lo, hi)
                 continue
-            out.append({"dst_start": lo, "dst_end": hi, "delta": delta})
+            out.append({"dst_start": lo, "dst_end": hi, "delta": delta,
+                        "gen": int(ld.get("gen", -1))})
         return out
+
+    def _cover(self, load: dict):
+        """What answers coverage for ``load``: the store, or one generation of it."""
+        if not self._extents:
+            return self._store
+        return _GenCover(self._store, int(load.get("gen", -1)))
 
     def get_num_new_matched_tokens(self, request: Request,
                                    num_computed_tokens: int) -> tuple[int | None, bool]:
@@ -256,13 +284,17 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             return max(gp.filled_tokens - num_computed_tokens, 0), False
 
         req = params.get("load")
-        decision, why = plan_load(self._store, session, req, num_computed_tokens,
+        if self._extents and req and "gen" not in req:
+            logger.warning("shift: extent store needs the load's generation; recomputing")
+            return 0, False
+        decision, why = plan_load(self._cover(req or {}), session, req, num_computed_tokens,
                                   request.num_prompt_tokens, self._bs)
         if decision is None:
             if session and req:
                 logger.warning("shift: session %s declining reuse: %s", session, why)
             return 0, False
-        self._plans[request.request_id] = (decision.lo, decision.hi, decision.delta)
+        self._plans[request.request_id] = (decision.lo, decision.hi, decision.delta,
+                                           int(req.get("gen", -1)))
         return decision.hi - decision.lo, False
 
     def update_state_after_alloc(self, request: Request, blocks: KVCacheBlocks,
@@ -282,6 +314,18 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         if not blocks:
             return
         params = self._params.get(rid) or {}
+        if self._extents:
+            # only what this step computed is saved, tagged with the turn's
+            # generation; reused spans keep the rows of the turn that made them
+            gen = params.get("gen")
+            if not session or not params.get("save") or hi <= lo:
+                return
+            if gen is None or not self._store.save_extent(session, int(gen), lo, hi - lo):
+                logger.warning("shift: session %s refused save of [%d,%d) (generation %s)",
+                               session, lo, hi, gen)
+                return
+            meta.saves.append(_Save(session, lo, hi - lo, list(blocks), self._bs, int(gen)))
+            return
         window = plan_save(self._store, session, params.get("save"), lo, hi)
         if window is None:
             if session and params.get("save") and hi > lo:
@@ -298,17 +342,22 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             rid = req.req_id
             self._blocks[rid] = list(req.block_ids[0])
             session = self._table.session_of(rid) or ""
+            if self._extents and session:
+                for g, p0, n in (self._params.get(rid) or {}).get("release", ()):
+                    self._store.release(session, int(g), int(p0), int(n))
+                    meta.releases.append((session, int(g), int(p0), int(n)))
             if rid in self._need_load and rid in self._multi:
                 table = list(self._blocks[rid])  # one block table shared by the segments
                 for seg in self._multi[rid]:
                     n = seg["dst_end"] - seg["dst_start"]
                     meta.loads.append(_Load(session, seg["dst_start"] - seg["delta"],
-                                            seg["delta"], seg["dst_start"], n, table, self._bs))
+                                            seg["delta"], seg["dst_start"], n, table, self._bs,
+                                            seg.get("gen", -1)))
                 self._need_load.discard(rid)
             elif rid in self._need_load:
-                lo, hi, delta = self._plans[rid]
+                lo, hi, delta, gen = self._plans[rid]
                 meta.loads.append(_Load(session, lo - delta, delta, lo, hi - lo,
-                                        list(self._blocks[rid]), self._bs))
+                                        list(self._blocks[rid]), self._bs, gen))
                 self._need_load.discard(rid)
             lo = req.num_computed_tokens
             self._plan_save(meta, rid, lo, lo + scheduler_output.num_scheduled_tokens[rid])
@@ -379,7 +428,11 @@ class MarathonShiftConnector(KVConnectorBase_V1):
 
     def start_load_kv(self, forward_context: ForwardContext, **kwargs: Any) -> None:
         meta = self._get_connector_metadata()
-        if not isinstance(meta, ShiftConnectorMetadata) or not meta.loads:
+        if not isinstance(meta, ShiftConnectorMetadata):
+            return
+        for session, g, p0, n in meta.releases:  # mirrors the scheduler's releases
+            self._store.release(session, g, p0, n)
+        if not meta.loads:
             return
         if not self._worker.registered:
             caches = {
@@ -393,8 +446,11 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._worker.k_scales = self._k_scales(forward_context)
             if self._worker.k_scales is not None:
                 self._worker.k_scales = self._worker.k_scales.to(self._worker.layers.device)
-        jobs = [LoadJob(ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length,
-                        block_ids=ld.block_ids) for ld in meta.loads]
+        if self._extents:
+            jobs = self._extent_load_jobs(meta.loads)
+        else:
+            jobs = [LoadJob(ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length,
+                            block_ids=ld.block_ids) for ld in meta.loads]
         # a store off the GPU streams in layer by layer behind the forward pass
         # (wait_for_layer_load orders each layer's attention after its rows);
         # a device store loads synchronously, as the reference did
@@ -415,10 +471,30 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         else:
             logger.info("shift: %d load(s) in one launch, copy_ms=%.2f (%.2f MB, %.1f GB/s)",
                         len(done), ms, moved / 2**20, moved / 2**30 / max(ms / 1e3, 1e-9))
-        if VERIFY_LOAD:
+        if VERIFY_LOAD and not self._extents:
             for j in done:
                 self._verify(j)
         logger.info("shift: store %s", self._store.stats())
+
+    def _extent_load_jobs(self, loads: list[_Load]) -> list[LoadJob]:
+        """A load of generation ``gen``'s positions as one job per store extent."""
+        jobs = []
+        for ld in loads:
+            where = self._store.locate(ld.session, ld.gen, ld.src_start, ld.length, count=False)
+            if where is None:
+                logger.error("shift: session %s generation %d lost [%d,%d); load skipped",
+                             ld.session, ld.gen, ld.src_start, ld.src_start + ld.length)
+                continue
+            for p0, n, row in where:
+                jobs.append(LoadJob(ld.session, p0, ld.delta, p0 + ld.delta, n,
+                                    block_ids=ld.block_ids, store_start=row))
+        return jobs
+
+    def _extent_save_jobs(self, save: _Save) -> list[SaveJob]:
+        """This step's fresh positions as one job per extent (the scheduler's allocation)."""
+        return [SaveJob(save.session, p0, n, block_ids=save.block_ids, store_start=row)
+                for p0, n, row in self._store.save_extent(save.session, save.gen,
+                                                         save.dst_start, save.length)]
 
     def _verify(self, job: LoadJob) -> None:
         """Read a loaded span back and compare it with a torch fp32 re-rotation."""
@@ -475,6 +551,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
 
     def _save_layers(self, names: list[str], meta: ShiftConnectorMetadata) -> None:
         jobs = []
+        if self._extents:
+            for save in meta.saves:
+                jobs.extend(self._extent_save_jobs(save))
+            if jobs:
+                self._worker.save(jobs, names, check=False)
+            return
         for save in meta.saves:
             # mirrors the scheduler's reserve for this step; idempotent across layers
             if not self._store.reserve(save.session, save.dst_start, save.length):
@@ -505,6 +587,9 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._save_layers_batched(group, meta)
 
     def _save_layers_batched(self, names: list[str], meta: ShiftConnectorMetadata) -> None:
+        if self._extents:
+            self._save_layers(names, meta)
+            return
         jobs = []
         for save in meta.saves:
             if not self._store.reserve(save.session, save.dst_start, save.length):

@@ -30,7 +30,12 @@ logger = logging.getLogger("vllm.marathon_shift")
 
 @dataclass
 class LoadJob:
-    """One load: store ``[src_start, +length)`` -> logical ``[dst_start, +length)``."""
+    """One load: store ``[src_start, +length)`` -> logical ``[dst_start, +length)``.
+
+    ``store_start`` names the first store row when rows are not addressed by
+    position (an :class:`~marathon_b200.extent_store.ExtentStore`); by
+    default it is ``src_start``.
+    """
 
     session: str
     src_start: int
@@ -39,6 +44,11 @@ class LoadJob:
     length: int
     block_ids: list[int] | np.ndarray | None = None
     slots: torch.Tensor | None = None  # alternative to block_ids: flat slots
+    store_start: int | None = None
+
+    @property
+    def row(self) -> int:
+        return self.src_start if self.store_start is None else self.store_start
 
     def host_slots(self, block_size: int) -> torch.Tensor:
         if self.slots is not None:
@@ -49,13 +59,19 @@ class LoadJob:
 
 @dataclass
 class SaveJob:
-    """One save: logical positions ``[dst_start, +length)`` -> the same store rows."""
+    """One save: logical positions ``[dst_start, +length)`` -> the same store rows
+    (or the rows from ``store_start``, for an extent store)."""
 
     session: str
     dst_start: int
     length: int
     block_ids: list[int] | np.ndarray | None = None
     slots: torch.Tensor | None = None
+    store_start: int | None = None
+
+    @property
+    def row(self) -> int:
+        return self.dst_start if self.store_start is None else self.store_start
 
 
 def _run(row: int, store_start: int, length: int, delta: int, block_ids, slots, paged_start,
@@ -140,8 +156,7 @@ class ShiftWorker:
         name_set = self._name_set
         accepted: list[LoadJob] = []
         for job in jobs:
-            missing = self.store.loadable(job.session, names, job.src_start, job.length,
-                                          name_set)
+            missing = self.store.loadable(job.session, names, job.row, job.length, name_set)
             if missing is not None:
                 logger.error("shift: session %s has no stored KV for %s; load skipped",
                              job.session, missing)
@@ -155,7 +170,7 @@ class ShiftWorker:
         tables: dict = {}
         for job in accepted:
             row = rows.setdefault(job.session, len(rows))
-            runs.append(_run(row, job.src_start, job.length, job.delta, job.block_ids, job.slots,
+            runs.append(_run(row, job.row, job.length, job.delta, job.block_ids, job.slots,
                              job.dst_start, tables))
         view = self.store.view(list(rows), names)
         if self.mover is not None and asynchronous:
@@ -208,10 +223,10 @@ class ShiftWorker:
             if not self.store.ensure_layers(job.session, names, geo.heads, 2 * geo.head_size,
                                             dtype):
                 continue
-            if job.dst_start + job.length > self.store.capacity(job.session):
+            if job.row + job.length > self.store.capacity(job.session):
                 continue
             row = rows.setdefault(job.session, len(rows))
-            runs.append(_run(row, job.dst_start, job.length, 0, job.block_ids, job.slots,
+            runs.append(_run(row, job.row, job.length, 0, job.block_ids, job.slots,
                              job.dst_start, tables))
         if not runs:
             return 0

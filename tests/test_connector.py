@@ -104,6 +104,50 @@ def test_first_turn_saves_then_edit_turn_loads_shifted():
     assert (meta2.saves[0].dst_start, meta2.saves[0].length) == (1100, 1)
 
 
+def test_extent_mode_saves_only_fresh_tokens_and_loads_by_generation():
+    """``store_mode="extents"``: the reused tail keeps its generation-0 rows, the
+    turn saves only what it computed, and a later turn loads from both."""
+    from marathon_b200.extent_store import AddressBook
+
+    conn = scheduler({"store_tokens": 65536, "store_mode": "extents"})
+    book = AddressBook()
+    # turn 0 (generation 0): 1000 tokens computed and saved
+    r0 = request("r0", {"session": "s", "save": True, "gen": 0}, 1000)
+    conn.on_new_request(r0)
+    blocks0 = list(range(100, 100 + 63))
+    meta = conn.build_connector_meta(sched_output([new_req("r0", blocks0, 0)],
+                                                  scheduled={"r0": 1000}))
+    assert [(sv.gen, sv.dst_start, sv.length) for sv in meta.saves] == [(0, 0, 1000)]
+    conn.request_finished(r0, blocks0)
+    assert book.after_turn([], 1000, 0) == []
+
+    # turn 1 (generation 1): [200, 240) replaced by 64 tokens, tail [240, 1000) -> +24
+    segs = [{"dst_start": 0, "dst_end": 200, "delta": 0},
+            {"dst_start": 264, "dst_end": 1024, "delta": 24}]
+    loads = book.loads(segs)
+    dead = book.after_turn(segs, 1100, 1)
+    r1 = request("r1", {"session": "s", "load": loads[1], "save": True, "gen": 1,
+                        "release": [list(d) for d in dead]}, 1100)
+    conn.on_new_request(r1)
+    n, _ = conn.get_num_new_matched_tokens(r1, 192)  # vLLM's own prefix hit
+    assert n == 0  # the load starts at 264, above the prefix hit: declined
+    n, _ = conn.get_num_new_matched_tokens(r1, 272)
+    assert n == 1024 - 272
+    conn.update_state_after_alloc(r1, None, n)
+    blocks1 = list(range(300, 300 + 69))
+    meta = conn.build_connector_meta(sched_output([new_req("r1", blocks1, 1024)],
+                                                  scheduled={"r1": 1100 - 1024}))
+    assert meta.releases == [("s", 0, 200, 40)]
+    ld = meta.loads[0]
+    assert (ld.gen, ld.src_start, ld.delta, ld.dst_start, ld.length) == (0, 248, 24, 272, 752)
+    # only the computed tail is saved, as generation 1 (no "full" rewrite)
+    assert [(sv.gen, sv.dst_start, sv.length) for sv in meta.saves] == [(1, 1024, 76)]
+    st = conn._store
+    assert st.locate("s", 0, 200, 40, count=False) is None  # released
+    assert st.locate("s", 0, 240, 760, count=False) is not None  # generation 0 intact
+    conn.request_finished(r1, blocks1)
+
+
 def test_load_is_declined_not_guessed_when_the_store_lost_the_source():
     conn = scheduler({"store_tokens": 4096})
     r = request("a", {"session": "x", "load": {"dst_start": 64, "dst_end": 640, "delta": 8}},
@@ -240,3 +284,73 @@ def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, b
     s = conn._store.stats()
     assert s["loaded_token_layers"] == 528 * L
     assert s["saved_token_layers"] == 600 * L
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("store_device", ["cuda", "cpu"])
+def test_extent_mode_three_turns_load_from_generation_zero(cuda, store_device):
+    """Three turns through the worker hooks in ``store_mode="extents"``: the last
+    turn loads spans first computed in turns 0 and 1, each rotated once from
+    the bytes of the turn that computed it (bit-exact against the oracle)."""
+    from oracle import shift_oracle as O
+
+    H, D, L, NBLK = 8, 128, 3, 160
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192, "store_mode": "extents",
+                                                 "store_device": store_device}),
+                                    KVConnectorRole.WORKER, None)
+    g = torch.Generator().manual_seed(3)
+    caches = {f"model.layers.{i}.self_attn.attn":
+              torch.randn(NBLK, BS, H, 2 * D, generator=g).to(torch.bfloat16).to(cuda)
+              for i in range(L)}
+    conn.register_kv_caches(caches)
+    perm = np.random.default_rng(4).permutation(NBLK)
+    bt = [perm[0:40].tolist(), perm[40:80].tolist(), perm[80:120].tolist()]
+    ctx = SimpleNamespace(no_compile_layers={}, virtual_engine=0)
+
+    def rows(kv, blocks, lo, hi):  # [n, H, 2D] bits of positions [lo, hi)
+        pos = np.arange(lo, hi)
+        blk = np.asarray(blocks)[pos // BS]
+        return kv.cpu().view(torch.int16).numpy().view(np.uint16)[blk, pos % BS]
+
+    def step(meta, save=True):
+        conn.bind_connector_metadata(meta)
+        conn.start_load_kv(ctx)
+        for name in caches:
+            conn.wait_for_layer_load(name)
+        if save:
+            for name, kv in caches.items():
+                conn.save_kv_layer(name, kv, None)
+        conn.wait_for_save()
+        conn.clear_connector_metadata()
+        torch.cuda.synchronize()
+
+    # turn 0: positions [0, 600) computed and saved as generation 0
+    step(C.ShiftConnectorMetadata(saves=[C._Save("s", 0, 600, bt[0], BS, 0)]))
+    gen0 = {n: rows(kv, bt[0], 0, 600) for n, kv in caches.items()}
+    # turn 1: [0, 100) replaced by 137 fresh tokens (generation 1); [100, 600) -> +37
+    step(C.ShiftConnectorMetadata(
+        loads=[C._Load("s", 100, 37, 137, 500, bt[1], BS, 0)],
+        saves=[C._Save("s", 0, 137, bt[1], BS, 1)],
+        releases=[("s", 0, 0, 100)]))
+    gen1 = {n: rows(kv, bt[1], 0, 137) for n, kv in caches.items()}
+    # turn 2: [0, 50) deleted: generation 1's [50, 137) -> [0, 87) by -50 and
+    # generation 0's [100, 600) -> [87, 587): one rotation of -13 from turn 0's bytes
+    step(C.ShiftConnectorMetadata(
+        loads=[C._Load("s", 50, -50, 0, 87, bt[2], BS, 1),
+               C._Load("s", 100, -13, 87, 500, bt[2], BS, 0)],
+        releases=[("s", 1, 0, 50)]), save=False)
+
+    inv = conn._inv_freq.numpy()
+    t50, t13 = O.rope_tables([-50, -13], inv)
+    for name, kv in caches.items():
+        got = rows(kv, bt[2], 0, 587)
+        want1 = gen1[name][50:137]
+        want0 = gen0[name][100:600]
+        assert np.array_equal(got[:87, :, D:], want1[..., D:])
+        assert np.array_equal(got[:87, :, :D], O.shift_k_bits(want1[..., :D], t50, O.BF16))
+        assert np.array_equal(got[87:, :, D:], want0[..., D:])
+        assert np.array_equal(got[87:, :, :D], O.shift_k_bits(want0[..., :D], t13, O.BF16))
+    st = conn._store
+    assert st.locate("s", 0, 0, 100, count=False) is None
+    assert st.locate("s", 1, 0, 50, count=False) is None
+    assert st.locate("s", 0, 100, 500, count=False) is not None
