@@ -107,3 +107,25 @@ def test_scatter_shifted_operator_matches_the_function(cuda):
     torch.cuda.synchronize()
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
     assert not torch.equal(a.view(torch.int16), kv[0].to(cuda).view(torch.int16))
+
+
+@pytest.mark.gpu
+def test_operators_trace_under_torch_compile(cuda):
+    """Dynamo traces through the operators (their fake implementations) and the
+    compiled call mutates the caches exactly as the eager call does."""
+    stores, kv, tables, seg = _case(cuda, seed=7)
+    inv = sk.inv_freq(D, 1e6).to(cuda)
+    st_d = [t.to(cuda) for per in stores for t in per]
+    bt_d = [torch.from_numpy(t).to(cuda) for t in tables]
+    segs = torch.tensor(seg)
+    a = [t.to(cuda) for t in kv]
+    b = [t.to(cuda) for t in kv]
+
+    def step(caches):
+        torch.ops.marathon.shift_load(st_d, caches, segs, bt_d, inv, BS, "nhd", None)
+
+    torch.compile(step, backend="eager", fullgraph=True)(a)
+    step(b)
+    torch.cuda.synchronize()
+    for x, y in zip(a, b, strict=True):
+        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
