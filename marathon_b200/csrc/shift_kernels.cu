@@ -438,6 +438,10 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 
     const bool rotate = !SAVE && HALF > 0 && tab != nullptr && g < NP;
     const int nu = nt * a.heads;
+    // units in the order of the side being written, so neighbouring threads
+    // store neighbouring rows: a load writes the paged cache, head-major when a
+    // head's tokens are adjacent there (HND); a save writes the token-major store
+    const bool head_major = !SAVE && a.head_stride > a.off_stride;
     const int64_t row0 = run.store_start + t0;
     constexpr int U = MSHIFT_UNITS;
     for (int u = u_first; u < nu; u += U * UPP) {
@@ -452,8 +456,14 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
         const int uu = u + q * UPP;
         live[q] = false;
         if (uu < nu) {
-          const int t = uu / a.heads;
-          const int h = uu - t * a.heads;
+          int t, h;
+          if (head_major) {
+            h = uu / nt;
+            t = uu - h * nt;
+          } else {
+            t = uu / a.heads;
+            h = uu - t * a.heads;
+          }
           const int64_t off = s_off[t];
           if (off >= 0) {
             live[q] = true;
