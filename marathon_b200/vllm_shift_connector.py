@@ -29,10 +29,11 @@ What changes is the worker side:
   ``wait_for_save`` and run as one launch over all layers.
 * ``store_device`` other than this worker's GPU (``"cpu"``: pinned host
   memory, or another GPU) keeps the store off the GPU; loads are staged
-  through a device ring and, unless ``async_tier_load`` is false, run on
-  their own streams while the forward pass proceeds: ``wait_for_layer_load``
-  orders each layer's attention after its rows, ``wait_for_save`` checks the
-  load's status.
+  through a device ring and run on their own streams while the forward pass
+  proceeds: ``wait_for_layer_load`` orders each layer's attention after its
+  rows.  For any store, the load's status is checked in ``wait_for_save``
+  rather than by blocking ``start_load_kv`` (``async_tier_load: false`` or
+  ``MARATHON_VERIFY_LOAD=1`` restore the blocking load).
 
 Paged layouts: the fused 4-D layouts the reference asserts (NHD/HND,
 ``:393-402``) and the 5-D split layouts of vLLM 0.22's FlashAttention
@@ -451,10 +452,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         else:
             jobs = [LoadJob(ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length,
                             block_ids=ld.block_ids) for ld in meta.loads]
-        # a store off the GPU streams in layer by layer behind the forward pass
+        # the load is queued and its status checked in wait_for_save: a store
+        # off the GPU streams in layer by layer behind the forward pass
         # (wait_for_layer_load orders each layer's attention after its rows);
-        # a device store loads synchronously, as the reference did
-        staged = self._worker.mover is not None and self._async_tier and not VERIFY_LOAD
+        # a device store's load runs on the forward pass's own stream, ahead
+        # of it, without the host waiting for it as the reference did
+        staged = self._async_tier and not VERIFY_LOAD
         t0 = time.perf_counter()
         done = self._worker.load(jobs, check=True, asynchronous=staged)
         ms = (time.perf_counter() - t0) * 1e3
@@ -466,7 +469,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                         "delta=%d", j.session, j.length, len(self._worker.layers), j.src_start,
                         j.src_start + j.length, j.delta)
         if staged:
-            logger.info("shift: %d load(s) queued from the %s store tier (%.2f MB, %.2f ms "
+            logger.info("shift: %d load(s) queued from the %s store (%.2f MB, %.2f ms "
                         "to queue)", len(done), self._store.device, moved / 2**20, ms)
         else:
             logger.info("shift: %d load(s) in one launch, copy_ms=%.2f (%.2f MB, %.1f GB/s)",

@@ -112,7 +112,7 @@ class ShiftWorker:
         # a store in host memory or on another GPU is reached by staged copies
         self.chunk_bytes = int(chunk_bytes)
         self.mover: StagedMover | None = None
-        self.pending: StagedLoad | None = None  # an asynchronous staged load in flight
+        self.pending: StagedLoad | None = None  # an asynchronous load in flight
 
     @property
     def registered(self) -> bool:
@@ -142,10 +142,12 @@ class ShiftWorker:
         the first missing layer (``vllm_shift_connector.py:506-513``): jobs
         before it are loaded, it and later ones are not.
 
-        ``asynchronous`` (a store off the GPU only): the staged load runs on
-        its own streams and this returns once it is queued; ``wait_layer``
-        orders a layer's consumers after its rows, ``finish_pending`` checks
-        the outcome.  On a device store the load is synchronous regardless.
+        ``asynchronous``: return once the load is queued, with its status
+        checked later by ``finish_pending``.  A store off the GPU is staged on
+        the mover's own streams (``wait_layer`` orders a layer's consumers
+        after its rows); a device store's load is queued on the current
+        stream, so later work on that stream is ordered after it anyway and
+        only the host-side status check is deferred.
         """
         if not jobs:
             return []
@@ -176,9 +178,25 @@ class ShiftWorker:
         if self.mover is not None and asynchronous:
             self.pending = self.mover.load_async(runs, view, self.inv, k_scales=self.k_scales)
             return accepted
+        if asynchronous:
+            self.pending = self._queue_load(runs, view)
+            return accepted
         mover = self.mover or self.launcher
         mover.load(runs, view, self.inv, k_scales=self.k_scales, check=check)
         return accepted
+
+    def _queue_load(self, runs, view) -> StagedLoad:
+        """One launch on the current stream; its status word is copied back
+        asynchronously and read in ``finish_pending``."""
+        la = self.launcher
+        p = la.prepare_load(runs, view, self.inv, k_scales=self.k_scales)
+        la.launch(p)
+        errs = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        la.staging.copy_err(p.slot, errs, p.stream)
+        la.finish(p, False)
+        done = torch.cuda.Event()
+        done.record(p.stream)
+        return StagedLoad([done] * len(self.layers), done, errs, 1)
 
     def wait_layer(self, name: str) -> None:
         """Order the current stream after layer ``name`` of a pending staged load."""
@@ -186,7 +204,7 @@ class ShiftWorker:
             self.pending.wait_layer(self.layers.index[name])
 
     def finish_pending(self) -> None:
-        """Complete a pending staged load: the current stream waits for all of it,
+        """Complete a pending load: the current stream waits for all of it,
         the host checks its status (raises :class:`ShiftError` on rejected tokens)."""
         job, self.pending = self.pending, None
         if job is not None:

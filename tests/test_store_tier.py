@@ -280,3 +280,24 @@ def test_host_tier_async_load_reports_bad_slots_at_finish(cuda):
     with pytest.raises(ShiftError, match="slot outside"):
         worker.finish_pending()
     assert worker.pending is None
+
+
+@pytest.mark.gpu
+def test_device_store_queued_load_checks_status_at_finish(cuda):
+    """A device store's asynchronous load: same bits as the blocking load, and a
+    rejected token surfaces at ``finish_pending``."""
+    a_w, a_kv, _, jobs, _ = _case(cuda, str(cuda), seed=17)
+    b_w, b_kv, _, bjobs, _ = _case(cuda, str(cuda), seed=17)
+    a_w.load(jobs, asynchronous=True)
+    assert a_w.pending is not None
+    b_w.load(bjobs)
+    a_w.finish_pending()
+    torch.cuda.synchronize()
+    for x, y in zip(a_kv, b_kv, strict=True):
+        assert np.array_equal(_bits(x), _bits(y))
+    bad = jobs[2].slots.clone()
+    bad[3] = 48 * BS + 1
+    jobs[2].slots = bad
+    a_w.load(jobs, asynchronous=True)
+    with pytest.raises(ShiftError, match="slot outside"):
+        a_w.finish_pending()
