@@ -188,3 +188,44 @@ def test_thirty_front_edits_keep_every_coordinate_exact():
     for _ in range(31):
         h.turn("front")
     assert h.loads_checked >= 30
+
+
+def test_scheduler_mirror_and_worker_store_stay_identical_under_eviction():
+    """The two copies see the same operations in the same order (the scheduler
+    checks coverage and plans saves; the worker applies releases, loads and
+    saves) and so allocate identical rows, evictions included."""
+    rng = np.random.default_rng(5)
+    sched = ExtentStore(6000, device="cpu", allocate=False, slab=512)
+    work = ExtentStore(6000, device="cpu", allocate=False, slab=512)
+    held: dict[str, list[tuple[int, int, int]]] = {}
+    for step in range(300):
+        s = f"s{int(rng.integers(0, 6))}"
+        gen = step
+        # a load of something this session saved earlier (if still held)
+        if held.get(s):
+            g, p0, n = held[s][int(rng.integers(0, len(held[s])))]
+            a = sched.locate(s, g, p0, n)  # scheduler coverage check (touches)
+            if a is not None:
+                b = work.locate(s, g, p0, n, count=False)
+                assert a == b
+                work.mark_loaded(s, ["l0"], n)  # the worker's touch for the load
+        # a release of one old extent, then this step's save
+        if held.get(s) and rng.random() < 0.4:
+            g, p0, n = held[s].pop(0)
+            assert sched.release(s, g, p0, n) == work.release(s, g, p0, n)
+        p0, n = int(rng.integers(0, 4000)), int(rng.integers(1, 800))
+        a = sched.save_extent(s, gen, p0, n)
+        b = work.save_extent(s, gen, p0, n)
+        assert a == b
+        if a:
+            held.setdefault(s, []).append((gen, p0, n))
+        for name in list(held):
+            if name not in sched._sessions:
+                held.pop(name)
+        assert list(sched._sessions) == list(work._sessions)
+        for name in sched._sessions:
+            x, y = sched._sessions[name], work._sessions[name]
+            assert x.capacity == y.capacity and x.free == y.free
+            assert {g: [(e.pos0, e.n, e.row) for e in v] for g, v in x.extents.items()} == \
+                {g: [(e.pos0, e.n, e.row) for e in v] for g, v in y.extents.items()}
+    assert sched.evictions > 0 and sched.evictions == work.evictions
