@@ -40,14 +40,22 @@ _launchers: dict = {}
 
 
 def _launcher(kv: list[torch.Tensor], block_size: int, layout: str) -> Launcher:
-    """One launcher per registered set of cache tensors (their pointers are staged once)."""
-    key = (tuple((t.data_ptr(), tuple(t.shape), t.dtype) for t in kv), block_size, layout)
+    """One launcher per set of cache addresses and shapes (their pointers are staged once).
+
+    The cached launcher keeps only the addresses, not the tensors: a cache the
+    caller frees is freed, and a later cache at the same addresses with the
+    same shape, strides and dtype is served by the same launcher.
+    """
+    key = (tuple((t.data_ptr(), tuple(t.shape), t.stride(), t.dtype) for t in kv), block_size,
+           layout)
     la = _launchers.get(key)
     if la is None:
         if len(_launchers) > 16:
             _launchers.clear()
         fp8 = kv[0].dtype in (torch.float8_e4m3fn, torch.uint8)
-        la = _launchers[key] = Launcher(KVLayers(list(kv), block_size, layout, fp8=fp8))
+        la = Launcher(KVLayers(list(kv), block_size, layout, fp8=fp8))
+        la.layers.tensors = []  # the kernels need the staged addresses only
+        _launchers[key] = la
     return la
 
 
