@@ -204,4 +204,4 @@ class KVLayers:
         self.index = {name: i for i, name in enumerate(self.names)}
 
     def __len__(self) -> int:
-        return len(self.tensors)
+        return len(self.names)
