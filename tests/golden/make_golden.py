@@ -43,7 +43,9 @@ DELTAS_F32 = [0, 1, -1, 17, -17, 566, -566, -1133, 6759]
 
 
 def _ref():
-    src = os.environ.get("MARATHON_REFERENCE", "/root/reference/src")
+    src = os.environ.get("MARATHON_REFERENCE")
+    if not src:
+        sys.exit("set MARATHON_REFERENCE to the reference checkout's src/ directory")
     sys.path.insert(0, src)
     from marathon import shift_kernels, shift_store  # noqa: PLC0415
     from marathon.kvshift import rerotate_keys  # noqa: PLC0415
