@@ -222,7 +222,8 @@ class StagedMover:
             if not store.ptrs[r.session].all():
                 raise ShiftError(f"run {i}: session row {r.session} lacks a layer buffer")
 
-    def _copies(self, ch: Chunk, runs: list[RunSpec], store: StoreView, row_bytes: int,
+    @staticmethod
+    def _copies(ch: Chunk, runs: list[RunSpec], store: StoreView, row_bytes: int,
                 base: int, to_slot: bool) -> np.ndarray:
         """The chunk's ranges as ``mshift_copy`` records (store <-> slot)."""
         n_p = len(ch.pieces)

@@ -301,3 +301,39 @@ def test_device_store_queued_load_checks_status_at_finish(cuda):
     a_w.load(jobs, asynchronous=True)
     with pytest.raises(ShiftError, match="slot outside"):
         a_w.finish_pending()
+
+
+def test_chunk_copies_and_slot_view_agree():
+    """The copy records of a chunk move exactly each piece's store rows of each
+    layer, and the slot view the kernel reads points at where they land."""
+    from marathon_b200.shift_kernels import RunSpec, StoreView
+    from marathon_b200.store_tier import StagedMover
+
+    rng = np.random.default_rng(2)
+    lengths = [190, 9, 97, 150]
+    runs = [RunSpec(i % 2, int(rng.integers(0, 100)), n, 5, block_table=np.arange(30),
+                    paged_start=0) for i, n in enumerate(lengths)]
+    n_layers = 3
+    ptrs = (np.arange(2 * n_layers, dtype=np.uint64).reshape(2, n_layers) + 1) * (1 << 30)
+    view = StoreView(ptrs, np.array([400, 400], np.int64), 8 * 256, 256)
+    base = 1 << 44
+    for chunk_rows in (10_000, 300, 64):
+        for ch in plan_chunks(lengths, ROW, n_layers, chunk_rows * ROW):
+            rec = StagedMover._copies(ch, runs, view, ROW, base, to_slot=True)
+            sv = StagedMover._slot_view(ch, base, view)
+            assert sv.ptrs.shape == (len(ch.pieces), ch.n_layers)
+            i = 0
+            for li in range(ch.n_layers):
+                for j, p in enumerate(ch.pieces):
+                    r = runs[p.run]
+                    want_src = int(view.ptrs[r.session, ch.first_layer + li]) + \
+                        (r.store_start + p.offset) * ROW
+                    assert int(rec["src"][i]) == want_src
+                    assert int(rec["dst"][i]) == int(sv.ptrs[j, li])  # kernel reads row 0
+                    assert int(rec["bytes"][i]) == p.length * ROW
+                    assert sv.caps[j] == p.length
+                    i += 1
+            assert i == len(rec)
+            # a save copies the other way over the same ranges
+            back = StagedMover._copies(ch, runs, view, ROW, base, to_slot=False)
+            assert np.array_equal(back["src"], rec["dst"]) and np.array_equal(back["dst"], rec["src"])
