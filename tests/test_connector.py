@@ -356,3 +356,22 @@ def test_extent_mode_three_turns_load_from_generation_zero(cuda, store_device):
     assert st.locate("s", 0, 0, 100, count=False) is None
     assert st.locate("s", 1, 0, 50, count=False) is None
     assert st.locate("s", 0, 100, 500, count=False) is not None
+
+
+def test_extent_mode_worker_splits_loads_and_saves_by_extent():
+    """Worker-side translation (no GPU): a load spanning two extents of a
+    generation becomes two jobs with their own store rows; a save gets the rows
+    the scheduler allocated for the same call."""
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192, "store_mode": "extents",
+                                                 "store_device": "cpu"}),
+                                    KVConnectorRole.WORKER, None)
+    st = conn._store
+    st.save_extent("s", 0, 0, 100)
+    st.save_extent("s", 1, 0, 50)  # another generation takes the next rows
+    st.save_extent("s", 0, 100, 60)  # generation 0 continues elsewhere
+    jobs = conn._extent_load_jobs([C._Load("s", 40, 12, 52, 100, [0, 1, 2], BS, 0)])
+    assert [(j.src_start, j.length, j.store_start, j.dst_start, j.delta) for j in jobs] == \
+        [(40, 60, 40, 52, 12), (100, 40, 150, 112, 12)]
+    saves = conn._extent_save_jobs(C._Save("s", 160, 30, [0, 1, 2], BS, 0))
+    assert [(j.dst_start, j.length, j.store_start) for j in saves] == [(160, 30, 210)]
+    assert conn._extent_load_jobs([C._Load("s", 0, 0, 0, 10, [0], BS, 7)]) == []  # unknown gen
