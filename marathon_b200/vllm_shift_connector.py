@@ -272,6 +272,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         params = self._params.get(request.request_id) or {}
 
         multi = params.get("loads")
+        if GAPFILL and session and multi and self._extents:
+            # a gap-filled step computes scattered positions; saving its range
+            # as one generation would tag loaded keys as fresh ones
+            logger.warning("shift: the extent store does not take single-request "
+                           "multi-segment loads; recomputing")
+            return 0, False
         if GAPFILL and session and multi:
             accepted = self._accept_multi(request, session, multi, num_computed_tokens)
             if not accepted:
