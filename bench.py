@@ -362,6 +362,14 @@ def native_arm(args) -> None:
     if args.layers:
         cfg = scaled(cfg, args.layers)
     h_lo, h_hi = head_shard(cfg.heads, rank, world)
+    # store rows of every session plus a paged cache of about the same size,
+    # per rank (bytes_per_token_layer counts a row twice: read and write)
+    need = sum(cfg.history) * cfg.layers * cfg.bytes_per_token_layer(h_hi - h_lo)
+    _, total = torch.cuda.mem_get_info(device)
+    if need > total:
+        raise SystemExit(f"{cfg.name} needs about {need / 1e9:.0f} GB per GPU at "
+                         f"{h_hi - h_lo} heads per rank, more than the GPU's "
+                         f"{total / 1e9:.0f} GB (run it over more GPUs)")
     wl = build(cfg, device, head_lo=h_lo, head_hi=h_hi, layout=args.layout)
     fp8 = cfg.dtype == "e4m3"
     layers = KVLayers(wl.kv, cfg.block_size, args.layout, fp8=fp8)
