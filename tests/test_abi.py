@@ -117,3 +117,20 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "nope.so")
     with pytest.raises(_lib.ShiftError, match="not built"):
         _lib.load()
+
+
+def test_stage_validates_before_touching_cuda(lib):
+    """``mshift_stage`` rejects malformed copy lists on the host (no CUDA call is
+    made for them, nor for empty or zero-byte lists)."""
+    import numpy as np
+
+    assert _lib.COPY_DTYPE.itemsize == 24  # mshift_copy: dst, src, bytes
+    assert lib.mshift_stage(None, 0, None) == _lib.OK
+    assert lib.mshift_stage(None, 1, None) == _lib.EINVAL
+    assert lib.mshift_stage(None, -1, None) == _lib.EINVAL
+    rec = np.zeros(2, dtype=_lib.COPY_DTYPE)
+    assert lib.mshift_stage(rec.ctypes.data, 2, None) == _lib.OK  # zero-byte ranges skipped
+    rec[1]["bytes"] = -16
+    assert lib.mshift_stage(rec.ctypes.data, 2, None) == _lib.EINVAL
+    rec[1] = (0, 4096, 16)  # bytes with a null destination
+    assert lib.mshift_stage(rec.ctypes.data, 2, None) == _lib.EINVAL
