@@ -463,9 +463,9 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         # (wait_for_layer_load orders each layer's attention after its rows);
         # a device store's load runs on the forward pass's own stream, ahead
         # of it, without the host waiting for it as the reference did
-        staged = self._async_tier and not VERIFY_LOAD
+        queued = self._async_tier and not VERIFY_LOAD
         t0 = time.perf_counter()
-        done = self._worker.load(jobs, check=True, asynchronous=staged)
+        done = self._worker.load(jobs, check=True, asynchronous=queued)
         ms = (time.perf_counter() - t0) * 1e3
         geo = self._worker.layers.geometry
         moved = sum(j.length for j in done) * len(self._worker.layers) * geo.heads * \
@@ -474,7 +474,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             logger.info("shift: session %s loaded %d tokens x %d layers from store[%d:%d], "
                         "delta=%d", j.session, j.length, len(self._worker.layers), j.src_start,
                         j.src_start + j.length, j.delta)
-        if staged:
+        if queued:
             logger.info("shift: %d load(s) queued from the %s store (%.2f MB, %.2f ms "
                         "to queue)", len(done), self._store.device, moved / 2**20, ms)
         else:
