@@ -576,7 +576,7 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._worker.save(jobs, names, check=False)
 
     def wait_for_save(self):
-        self._worker.finish_pending()  # an asynchronous staged load of this step
+        self._worker.finish_pending()  # this step's queued load: wait, check its status
         if not self._pending_saves:
             return
         meta = self._get_connector_metadata() if self.has_connector_metadata() else None
