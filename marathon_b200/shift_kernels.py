@@ -403,6 +403,7 @@ class Prepared:
     k_scales: torch.Tensor | None = None
     inv_freq: torch.Tensor | None = None
     stream: object = None  # the torch stream current when the batch was prepared
+    uploaded: object = None  # event after the descriptor copy, when it ran on the copy stream
 
 
 class Launcher:
@@ -428,6 +429,8 @@ class Launcher:
         props = torch.cuda.get_device_properties(self.device)
         self._grid = props.multi_processor_count * self.CTAS_PER_SM
         self.staging = _Staging(self.device, self.lib, staging_slots)
+        self._copy_stream = None
+        self._upload_events = [torch.cuda.Event() for _ in range(staging_slots)]
         self._tiles: dict = {}
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
@@ -435,6 +438,25 @@ class Launcher:
 
     #: resident CTAs of the load/save kernel per SM (register-limited, B200)
     CTAS_PER_SM = 2
+
+    #: copy a batch's descriptors on the launcher's own copy stream as soon as
+    #: they are packed: the copy then overlaps whatever the launch stream is
+    #: still running (the previous batch's kernels), and the launch stream waits
+    #: on an event instead of serialising the copy in front of the kernels
+    EARLY_UPLOAD = True
+
+    def _upload(self, slot: int, total: int, stream, upload_stream):
+        if upload_stream is not None or not self.EARLY_UPLOAD:
+            self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
+            return None
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(self.device)
+        # the slot's previous batch has finished (begin() waited for it), so
+        # the copy may run ahead of the launch stream
+        self.staging.upload(slot, total, self._copy_stream.cuda_stream)
+        ev = self._upload_events[slot]
+        ev.record(self._copy_stream)
+        return ev
 
     #: per-tile cost in (token, head) units: barriers, slot resolution, table staging
     TILE_OVERHEAD_UNITS = 16
@@ -566,11 +588,12 @@ class Launcher:
             )
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
+        uploaded = self._upload(slot, total, stream, upload_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
-                        base + o_deltas, len(deltas), total, tt, stream=stream)
+                        base + o_deltas, len(deltas), total, tt, stream=stream,
+                        uploaded=uploaded)
 
     def _prepare_small(self, kind, runs, store, deltas, first_layer, n_layers, stream,
                        upload_stream=None) -> Prepared:
@@ -637,11 +660,12 @@ class Launcher:
             struct.pack_into("<q", host, o_deltas + 8 * k, d)
         for key, bt in host_tables.items():
             host[tab_at[key] : tab_at[key] + bt.nbytes] = bt.view(np.uint8)
-        self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
+        uploaded = self._upload(slot, total, stream, upload_stream)
         self.last_h2d = total
         return Prepared(kind, slot, base, base + o_runs, n_runs, tiles, n_layers, first_layer,
                         base + o_ptrs, base + o_caps, S, store.st_tok, store.st_head,
-                        base + o_deltas, len(deltas), total, tt, stream=stream)
+                        base + o_deltas, len(deltas), total, tt, stream=stream,
+                        uploaded=uploaded)
 
     def prepare_load(
         self,
@@ -700,6 +724,8 @@ class Launcher:
 
     def launch(self, p: Prepared, *, tables: bool = True, main: bool = True) -> int:
         """Issue the native launches of a prepared batch; returns how many were issued."""
+        if p.uploaded is not None:
+            p.stream.wait_event(p.uploaded)
         stream = p.stream.cuda_stream
         n = 0
         if p.kind == "load":

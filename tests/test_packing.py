@@ -62,6 +62,7 @@ def _launcher(heads: int, small: int) -> Launcher:
     la.staging = _FakeStaging()
     la.last_h2d = 0
     la._SMALL = small
+    la.EARLY_UPLOAD = False  # no copy stream without a GPU
     return la
 
 
