@@ -182,6 +182,18 @@ MSHIFT_API int32_t mshift_default_tile_tokens(int32_t heads);
 #define MSHIFT_KERNEL_AUTO 2
 MSHIFT_API int mshift_set_load_kernel(int kind);
 
+/*
+ * Diagnostic hook for the TMA load kernel's timeout path, process-wide.
+ * rounds >= 0 bounds the first full-barrier wait of every consumer warp of
+ * every later TMA load launch to that many try_wait rounds (0: it gives up at
+ * once), so a test can make that wait run out on purpose: the launch then
+ * sets MSHIFT_EBIT_TIMEOUT, writes nothing more, waits (with the normal bound)
+ * for the bulk copies it already issued, and returns.  rounds < 0 restores the
+ * normal bound.  Returns the previous setting (-1 = normal).  No counterpart in
+ * the reference (its Triton kernel had no waits).
+ */
+MSHIFT_API int32_t mshift_debug_first_wait(int32_t rounds);
+
 /* 1 if (dtype, head_size, rotary) has a compiled kernel, else 0. */
 MSHIFT_API int mshift_supported(int32_t dtype, int32_t head_size, int32_t rotary);
 

@@ -18,7 +18,7 @@ import numpy as np
 LIB_PATH = Path(__file__).resolve().parent / "libmarathon_shift.so"
 
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETOOBIG = 0, 1, 2, 3, 4
-EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE = 1, 2, 4, 8
+EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE, EBIT_TIMEOUT = 1, 2, 4, 8, 16
 BF16, F16, F32, E4M3 = 0, 1, 2, 3
 KERNEL_LSU, KERNEL_BULK, KERNEL_AUTO = 0, 1, 2
 
@@ -37,6 +37,7 @@ EXPORTS = (
     "mshift_load_noalloc",
     "mshift_noalloc_max_deltas",
     "mshift_set_load_kernel",
+    "mshift_debug_first_wait",
     "mshift_stage",
     "mshift_enable_peer",
 )
@@ -126,6 +127,7 @@ _SIGNATURES = {
     ),
     "mshift_noalloc_max_deltas": (_I32, []),
     "mshift_set_load_kernel": (ctypes.c_int, [ctypes.c_int]),
+    "mshift_debug_first_wait": (_I32, [_I32]),
     "mshift_stage": (ctypes.c_int, [_P, _I32, _P]),
     "mshift_enable_peer": (ctypes.c_int, [_I32]),
 }
@@ -177,6 +179,7 @@ def describe_bits(bits: int) -> str:
         (EBIT_STORE, "store position outside the session buffer"),
         (EBIT_SESSION, "bad session index or missing store buffer"),
         (EBIT_TABLE, "bad rotation-table index"),
+        (EBIT_TIMEOUT, "a bulk copy did not complete in time; the launch stopped early"),
     ):
         if bits & bit:
             names.append(name)

@@ -298,6 +298,9 @@ struct KArgs {
   const float* tables;       // [n_tables][2][half]
   const float* k_scales;     // [n_layers] (E4M3 only)
   uint32_t* err;
+  // diagnostic hook of the TMA load kernel: 0 = normal; n > 0 bounds every
+  // consumer warp's first full-barrier wait to n - 1 rounds
+  uint32_t first_wait;
   // single run, single layer (runs == nullptr)
   mshift_run run0;
   void* store0;
@@ -586,11 +589,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait: false after kWaitLimit rounds (the caller flags and drains).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+// Bounded wait: false after `limit` rounds (the caller flags and drains), or
+// as soon as another warp of the CTA has aborted (`abort` non-null and set).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint32_t limit = kWaitLimit,
+                                          const volatile int* abort = nullptr) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+  }
   return false;
+}
+
+// The same wait taken by a whole warp: true only if every lane's wait
+// succeeded, so the warp's lanes always take the same branch afterwards.
+__device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit,
+                                               const volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, limit, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Whether any warp of the CTA has aborted, as one answer for the whole warp.
+__device__ __forceinline__ bool warp_saw_abort(const volatile int* abort) {
+  return __any_sync(0xffffffffu, *abort != 0);
+}
+
+// Named barrier 1 over the whole CTA (barrier 0 is __syncthreads); the
+// non-aligned form, entered after the warp has reconverged.
+__device__ __forceinline__ void cta_barrier_1(int threads) {
+  __syncwarp();
+  asm volatile("barrier.sync 1, %0;" ::"r"(threads) : "memory");
 }
 
 __device__ __forceinline__ void bulk_to_smem(void* dst, const void* src, uint32_t bytes,
@@ -668,7 +696,7 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  __syncthreads();  // the only CTA-wide barrier: the warps part ways below
+  __syncthreads();  // the warps part ways below and meet again only at the end
 
   if (warp == kBulkConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -687,13 +715,13 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
     int k = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
       const int s = k % NS;
+      if (warp_saw_abort(&s_abort)) break;  // a consumer warp gave up: issue nothing more
       if (k >= NS) {
-        const bool free_ok = mbar_wait(&s_empty[s], ((k / NS) - 1) & 1);
-        if (!free_ok) {
+        if (!warp_mbar_wait(&s_empty[s], ((k / NS) - 1) & 1, kWaitLimit, &s_abort)) {
           if (lane == 0) atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
           s_abort = 1;
+          break;
         }
-        if (s_abort) break;
       }
       const int w = item / parts;
       const int part = item - w * parts;
@@ -793,9 +821,13 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
         }
       }
     }
+    // Wait until every consumer warp has left its loop, then, if the launch
+    // was aborted, for the copy last issued into each stage (the only one a
+    // stage can still have in flight: a stage is refilled only after its
+    // consumers released it), with the full bound and no abort shortcut, so
+    // no copy is left writing shared memory when the CTA exits.
+    cta_barrier_1(kBulkThreads);
     if (s_abort && lane == 0) {
-      // wait (bounded) for the copies issued into each stage, so none is
-      // left writing shared memory when the CTA exits
       for (int kk = k - NS < 0 ? 0 : k - NS; kk < k; ++kk)
         (void)mbar_wait(&s_full[kk % NS], (kk / NS) & 1);
     }
@@ -814,11 +846,12 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
   int k = 0;
   for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
     const int s = k % NS;
-    if (!mbar_wait(&s_full[s], (k / NS) & 1)) {
+    const uint32_t limit = (k == 0 && a.first_wait != 0u) ? a.first_wait - 1u : kWaitLimit;
+    if (!warp_mbar_wait(&s_full[s], (k / NS) & 1, limit, &s_abort)) {
       if (lane == 0) atomicOr(a.err, MSHIFT_EBIT_TIMEOUT);
       s_abort = 1;
+      break;
     }
-    if (s_abort) break;
     const BulkMeta m = s_meta[s];
     const unsigned char* stage = s_data + s * stage_bytes;
     const int nu = m.nt * a.heads;
@@ -875,6 +908,7 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
     __syncwarp();
     if (lane == 0) mbar_arrive(&s_empty[s]);  // this warp is done reading stage s
   }
+  cta_barrier_1(kBulkThreads);  // the producer drains after every consumer is out
 }
 
 // cos/sin of fp32(delta) * inv_freq[i]: the angle is rounded to fp32 exactly
@@ -1041,6 +1075,10 @@ int variant_slot(const Variant* v, bool save) {
 // dequantise/requantise arithmetic, 128-bit loads for 16/32-bit types).
 std::atomic<int> g_load_kernel{MSHIFT_KERNEL_AUTO};
 
+// KArgs::first_wait of every batched load (0: normal waits); see
+// mshift_debug_first_wait.
+std::atomic<uint32_t> g_first_wait{0};
+
 // Launch the TMA bulk load; returns MSHIFT_EUNSUPPORTED when the geometry does
 // not fit a stage (the caller then uses the 128-bit-load kernel).
 int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStream_t stream,
@@ -1135,6 +1173,7 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   a.tables = save ? nullptr : tables;
   a.k_scales = save ? nullptr : k_scales;
   a.err = err;
+  a.first_wait = g_first_wait.load(std::memory_order_relaxed);
   const int64_t row_elems = (int64_t)paged->heads * 2 * paged->head_size;
   const int kind = g_load_kernel.load(std::memory_order_relaxed);
   const bool want_bulk =
@@ -1276,6 +1315,11 @@ int mshift_set_load_kernel(int kind) {
   if (kind != MSHIFT_KERNEL_LSU && kind != MSHIFT_KERNEL_BULK && kind != MSHIFT_KERNEL_AUTO)
     return -1;
   return g_load_kernel.exchange(kind);
+}
+
+int32_t mshift_debug_first_wait(int32_t rounds) {
+  const uint32_t prev = g_first_wait.exchange(rounds < 0 ? 0u : static_cast<uint32_t>(rounds) + 1u);
+  return prev == 0u ? -1 : static_cast<int32_t>(prev - 1u);
 }
 
 const char* mshift_version(void) { return "marathon_b200 shift 0.1 (sm_100a)"; }

@@ -251,18 +251,28 @@ def scatter_shifted(
         _raise_bits(take_errors(kv.device), "scatter_shifted")
 
 
-def warmup(kv: torch.Tensor, block_size: int, hnd: bool) -> None:
+def warmup(kv: torch.Tensor, block_size: int, hnd: bool, *, rotary: int | None = None,
+           layout: str | None = None, fp8: bool = False) -> None:
     """Load the library and validate ``kv``'s geometry before the first real load.
 
-    The reference JIT-compiled Triton here (``shift_kernels.py:213-238``); the
-    native kernels are compiled ahead of time, so nothing is compiled.
+    The reference JIT-compiled Triton here (``shift_kernels.py:213-238``) and
+    its connector called it from ``register_kv_caches``
+    (``vllm_shift_connector.py:405``), so a geometry no kernel serves failed at
+    registration rather than at the first load.  The native kernels are
+    compiled ahead of time: this loads the library and raises
+    :class:`ShiftError` when no compiled kernel serves ``kv``'s dtype, head
+    size and ``rotary`` (default: the whole head).  ``layout`` (``"nhd"``,
+    ``"hnd"``, ``"split"``, ``"split_blocks"``) overrides ``hnd`` for the 5-D
+    split caches; ``fp8`` marks a ``uint8`` cache as e4m3 codes.
     """
     lib = _lib.load()
     if not kv.is_cuda:
         return
-    geo = describe(kv, block_size, "hnd" if hnd else "nhd")
-    if not lib.mshift_supported(geo.dtype, geo.head_size, geo.head_size):
-        raise ShiftError(f"no kernel for dtype code {geo.dtype}, head_size {geo.head_size}")
+    geo = describe(kv, block_size, layout or ("hnd" if hnd else "nhd"), fp8=fp8)
+    rot = geo.head_size if rotary is None else int(rotary)
+    if not lib.mshift_supported(geo.dtype, geo.head_size, rot):
+        raise ShiftError(f"no kernel for dtype code {geo.dtype}, head_size {geo.head_size}, "
+                         f"rotary {rot}")
 
 
 # ------------------------------------------------------------------ batches
@@ -363,8 +373,14 @@ class _Staging:
                                          stream_ptr), "mshift_stage (descriptors)")
 
     def finish(self, slot: int, stream) -> None:
+        """The slot's latest use is queued on ``stream``: ``begin`` waits for it."""
         self.done[slot].record(stream)
         self.used[slot] = True
+
+    def drain(self) -> None:
+        for k in range(self.n):
+            if self.used[k]:
+                self.done[k].synchronize()
 
     def copy_err(self, slot: int, dst: torch.Tensor, stream) -> None:
         """Queue a copy of the slot's error word into ``dst`` (pinned int32 [1]) on ``stream``."""
@@ -446,8 +462,18 @@ class Launcher:
     EARLY_UPLOAD = True
 
     def _upload(self, slot: int, total: int, stream, upload_stream):
+        """Queue the slot's descriptor copy; returns the event a launch must wait on
+        (None when the copy is on the launch stream itself).
+
+        The slot counts as in use from here on, not only once its batch has
+        launched: a batch prepared and then abandoned still has a copy in flight
+        from the slot's pinned buffer, which the next ``begin`` of the slot
+        must wait for.
+        """
         if upload_stream is not None or not self.EARLY_UPLOAD:
-            self.staging.upload(slot, total, (upload_stream or stream).cuda_stream)
+            on = upload_stream or stream
+            self.staging.upload(slot, total, on.cuda_stream)
+            self.staging.finish(slot, on)
             return None
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(self.device)
@@ -456,7 +482,16 @@ class Launcher:
         self.staging.upload(slot, total, self._copy_stream.cuda_stream)
         ev = self._upload_events[slot]
         ev.record(self._copy_stream)
+        self.staging.finish(slot, self._copy_stream)
         return ev
+
+    def drain(self) -> None:
+        """Wait for every batch (and descriptor copy) issued from the staging slots.
+
+        Call before dropping a launcher: its pinned slots are read by raw
+        ``cudaMemcpyAsync`` calls the caching host allocator does not track.
+        """
+        self.staging.drain()
 
     #: per-tile cost in (token, head) units: barriers, slot resolution, table staging
     TILE_OVERHEAD_UNITS = 16
@@ -722,11 +757,18 @@ class Launcher:
             raise ShiftError(f"layer range [{first_layer}, +{n_layers}) outside the caches")
         return n_layers
 
-    def launch(self, p: Prepared, *, tables: bool = True, main: bool = True) -> int:
-        """Issue the native launches of a prepared batch; returns how many were issued."""
+    def launch(self, p: Prepared, *, tables: bool = True, main: bool = True,
+               err: int | None = None) -> int:
+        """Issue the native launches of a prepared batch; returns how many were issued.
+
+        The kernel ORs its rejected-token bits into the staging slot's status
+        word, or into the device word at address ``err`` when given (a word
+        the caller shares between several launches and reads once).
+        """
         if p.uploaded is not None:
             p.stream.wait_event(p.uploaded)
         stream = p.stream.cuda_stream
+        err_ptr = p.base if err is None else int(err)
         n = 0
         if p.kind == "load":
             half = int(p.inv_freq.numel())
@@ -747,7 +789,7 @@ class Launcher:
                         p.tables.data_ptr() if p.tables is not None else None, p.n_deltas,
                         p.k_scales.data_ptr() + 4 * p.first_layer
                         if p.k_scales is not None else None,
-                        p.base, stream,
+                        err_ptr, stream,
                     ),
                     "mshift_load",
                 )
@@ -760,7 +802,7 @@ class Launcher:
                         ctypes.byref(self.paged), p.runs, p.n_runs, p.tile_tokens, p.tiles,
                         p.n_layers, p.ptrs, p.caps, p.n_sessions, p.st_tok, p.st_head,
                         self.layers.k_ptrs.data_ptr() + off, self.layers.v_ptrs.data_ptr() + off,
-                        p.base, stream,
+                        err_ptr, stream,
                     ),
                     "mshift_save",
                 )
@@ -789,13 +831,14 @@ class Launcher:
         self.finish(p, check)
 
     def save(self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
-             n_layers: int | None = None, check: bool = True) -> None:
+             n_layers: int | None = None, check: bool = True, err: int | None = None) -> None:
         """Every run x layers ``[first_layer, +n_layers)``: paged rows -> store rows, bit copy.
 
-        ``store.ptrs`` has one column per layer of that range.
+        ``store.ptrs`` has one column per layer of that range.  ``err``: see
+        :meth:`launch` (only with ``check=False``).
         """
         if not runs:
             return
         p = self.prepare_save(runs, store, first_layer=first_layer, n_layers=n_layers)
-        self.launch(p)
-        self.finish(p, check)
+        self.launch(p, err=err)
+        self.finish(p, check and err is None)

@@ -186,6 +186,21 @@ class ShiftStore:
         entry.filled = need
         return True
 
+    def truncate(self, session: str, pos: int) -> None:
+        """Forget ``session``'s positions from ``pos`` on: a save there did not land.
+
+        The session keeps ``[base, min(filled, pos))``.  A later save that
+        starts above that is refused by :meth:`reserve` (it would leave a
+        hole), and a load reaching past it is declined by :meth:`covers`, so
+        the lost span is recomputed, never loaded.  Idempotent; the scheduler
+        mirror and the worker store apply the same truncations.  (The
+        reference has no such path: its saves were synchronous torch copies.)
+        """
+        entry = self._sessions.get(session)
+        if entry is None or entry.base < 0:
+            return
+        entry.filled = max(entry.base, min(entry.filled, int(pos)))
+
     def covers(self, session: str, start: int, n: int) -> bool:
         """Whether ``[start, start + n)`` is held for ``session`` (``shift_store.py:208-223``)."""
         entry = self._sessions.get(session)

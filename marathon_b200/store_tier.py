@@ -344,8 +344,12 @@ class StagedMover:
 
     # --------------------------------------------------------------- save
     def save(self, runs: list[RunSpec], store: StoreView, *, first_layer: int = 0,
-             n_layers: int | None = None, check: bool = True) -> None:
-        """Paged rows of every run x layers ``[first_layer, +n_layers)`` out to the store."""
+             n_layers: int | None = None, check: bool = True, err: int | None = None) -> None:
+        """Paged rows of every run x layers ``[first_layer, +n_layers)`` out to the store.
+
+        ``err``: a device status word every chunk's kernel ORs its rejected-token
+        bits into, read by the caller (with ``check=False``).
+        """
         if not runs:
             return
         n_layers = self.launcher.layer_range(first_layer, n_layers)
@@ -365,8 +369,9 @@ class StagedMover:
             p = self.launcher.prepare_save(self._piece_runs(ch, runs), view,
                                            first_layer=first_layer + ch.first_layer,
                                            n_layers=ch.n_layers)
-            self.launcher.launch(p)
-            self.launcher.staging.copy_err(p.slot, errs[ci : ci + 1], compute)
+            self.launcher.launch(p, err=err)
+            if err is None:
+                self.launcher.staging.copy_err(p.slot, errs[ci : ci + 1], compute)
             self.launcher.finish(p, False)
             gathered = torch.cuda.Event()
             gathered.record(compute)
@@ -380,7 +385,7 @@ class StagedMover:
         compute.wait_stream(self.copy_stream)  # later work on the stream sees the rows out
         self.last_chunks, self.last_copies = len(chunks), copies
         self.last_staged_bytes = sum(c.nbytes for c in chunks)
-        if check:
+        if check and err is None:
             self._raise(compute, errs, len(chunks), "staged shift save")
 
     @staticmethod

@@ -51,6 +51,8 @@ def _launcher(kv: list[torch.Tensor], block_size: int, layout: str) -> Launcher:
     la = _launchers.get(key)
     if la is None:
         if len(_launchers) > 16:
+            for old in _launchers.values():
+                old.drain()  # their pinned staging may still feed copies in flight
             _launchers.clear()
         fp8 = kv[0].dtype in (torch.float8_e4m3fn, torch.uint8)
         la = Launcher(KVLayers(list(kv), block_size, layout, fp8=fp8))

@@ -40,13 +40,29 @@ Paged layouts: the fused 4-D layouts the reference asserts (NHD/HND,
 ``(2, blocks, block_size, heads, head_size)`` and FlashInfer
 ``(blocks, 2, block_size, heads, head_size)``.  FP8 (e4m3) caches are
 dequantised, rotated and requantised with each layer's K scale.
+
+Failures are declined, never guessed at (the reference's rule,
+``:104-109``), on both directions of the data path:
+
+* a save the kernel refused (a bad slot, a store row out of range) is found
+  from the step's status word, read back without stalling the forward pass;
+  the session's store is truncated back to the start of that save on the
+  worker, and the scheduler's mirror does the same when it receives the
+  worker metadata (``build_connector_worker_meta`` ->
+  ``update_connector_output``), so the next turn recomputes that span;
+* a load that could not run (the store no longer holds the rows) or that the
+  kernel refused is reported through ``get_block_ids_with_load_errors``, which
+  makes vLLM recompute (or fail) those blocks instead of attending to them.
 """
 
 from __future__ import annotations
 
+import importlib
+import importlib.util
 import os
 import time
 from dataclasses import dataclass, field
+from pathlib import Path
 from typing import TYPE_CHECKING, Any
 
 import torch
@@ -57,8 +73,13 @@ from vllm.distributed.kv_transfer.kv_connector.v1.base import (
 )
 from vllm.logger import init_logger
 
-from . import gapfill
-from .shift_kernels import RopeShift, inv_freq as make_inv_freq, rope_shift
+try:  # the worker -> scheduler channel (vLLM >= 0.11)
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorWorkerMetadata
+except ImportError:  # pragma: no cover - older vLLM: failed saves stay worker-side
+    KVConnectorWorkerMetadata = object
+
+from . import _lib
+from .shift_kernels import RopeShift, ShiftError, inv_freq as make_inv_freq, rope_shift, warmup
 from .shift_store import (
     DEFAULT_STORE_TOKENS,
     SessionTable,
@@ -85,7 +106,8 @@ logger = init_logger("vllm.marathon_shift")
 #: (diagnostic, off by default; ``vllm_shift_connector.py:95-102``)
 VERIFY_LOAD = os.environ.get("MARATHON_VERIFY_LOAD", "") not in ("", "0")
 #: single-request multi-segment loads through a vLLM patched to honour a gap
-#: plan (``vllm_shift_connector.py:104-110``)
+#: plan (``vllm_shift_connector.py:104-110``); also ``"gapfill": true`` in
+#: the connector's extra config
 GAPFILL = os.environ.get("MARATHON_GAPFILL", "") not in ("", "0")
 #: defer per-layer saves to wait_for_save and run them as one launch
 BATCH_SAVE = os.environ.get("MARATHON_BATCH_SAVE", "") not in ("", "0")
@@ -98,18 +120,38 @@ _COUNTERS = ("hits", "misses", "evictions", "refusals", "loaded_token_layers",
 
 
 def stats() -> dict:
-    """Merged store counters across the connector instances of this process."""
-    out: dict[str, Any] = dict.fromkeys(_COUNTERS, 0)
-    out.update(sessions={}, used_tokens=0, budget_tokens=0)
-    for store in _STORES:
-        s = store.stats()
-        out["budget_tokens"] = s["budget_tokens"]
-        out["used_tokens"] = max(out["used_tokens"], s["used_tokens"])
-        for name, filled in s["sessions"].items():
-            out["sessions"][name] = max(out["sessions"].get(name, 0), filled)
-        for k in _COUNTERS:
-            out[k] += s[k]
-    return out
+    """Store counters of every connector instance in this process, merged.
+
+    Counters add up across instances; sizes (``used_tokens``, per-session
+    tokens) are the largest any instance reports, because the scheduler's
+    mirror and the worker's store describe the same sessions twice.  Same keys
+    as the reference's ``stats()`` (``vllm_shift_connector.py:121-136``).
+    """
+    snaps = [store.stats() for store in _STORES]
+    merged: dict[str, Any] = {k: sum(s[k] for s in snaps) for k in _COUNTERS}
+    sessions: dict[str, int] = {}
+    for snap in snaps:
+        for name, tokens in snap["sessions"].items():
+            sessions[name] = max(tokens, sessions.get(name, 0))
+    merged["sessions"] = sessions
+    merged["used_tokens"] = max((s["used_tokens"] for s in snaps), default=0)
+    merged["budget_tokens"] = snaps[-1]["budget_tokens"] if snaps else 0
+    return merged
+
+
+def ulp(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Unit in the last place of ``dtype`` at each fp32 value of ``x``.
+
+    ``2**(e - 1 - m)`` for ``|x|`` in ``[2**(e-1), 2**e)`` and ``m`` stored
+    mantissa bits (7 bf16, 10 fp16, 23 fp32); the subnormal spacing
+    ``tiny * eps`` below the normal range and at zero.
+    """
+    fi = torch.finfo(dtype)
+    mant = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}[dtype]
+    _, e = torch.frexp(x.abs().to(torch.float32))
+    step = torch.ldexp(torch.ones_like(x, dtype=torch.float32), e - 1 - mant)
+    floor = torch.full_like(step, fi.smallest_normal * fi.eps)
+    return torch.where(x == 0, floor, torch.maximum(step, floor))
 
 
 @dataclass
@@ -167,6 +209,100 @@ class _GenCover:
         return self.store.locate(session, self.gen, start, n) is not None
 
 
+@dataclass
+class ShiftWorkerMetadata(KVConnectorWorkerMetadata):
+    """Worker -> scheduler: store spans whose save did not land.
+
+    ``truncate`` holds ``(session, pos)`` for the flat store (positions from
+    ``pos`` on are forgotten), ``release`` holds ``(session, gen, pos0, n)``
+    for the extent store.  The scheduler's mirror applies the same change, so
+    its next ``plan_load`` declines rather than plan a load of rows that were
+    never written.  With tensor parallelism every rank reports its own; the
+    changes are idempotent, so the aggregate is the concatenation.
+    """
+
+    truncate: list[tuple[str, int]] = field(default_factory=list)
+    release: list[tuple[str, int, int, int]] = field(default_factory=list)
+
+    def aggregate(self, other: ShiftWorkerMetadata) -> ShiftWorkerMetadata:
+        return ShiftWorkerMetadata(self.truncate + other.truncate,
+                                   self.release + other.release)
+
+    def __bool__(self) -> bool:
+        return bool(self.truncate or self.release)
+
+
+class GapHandoff:
+    """The gap-fill hand-off to a vLLM patched to honour a non-prefix match.
+
+    vLLM's connector API can only report externally supplied KV as a prefix.
+    The reference's vLLM patch (``scripts/patch_vllm_gapfill.py``) changes
+    that for one request: its scheduler ``take``s the plan a connector
+    ``offer``ed on ``marathon.gapfill_channel`` and ``publish``es it, and its
+    model runner overwrites the request's positions with ``active()``'s
+    (``patch_vllm_gapfill.py:60-68``, ``:82-84``).  The plan itself is the
+    reference's ``marathon.gapfill.plan_gaps`` (``src/marathon/gapfill.py:82-106``).
+    Both are the reference's, consumed unchanged and imported by name: the
+    patch reads exactly that channel module, so offering anywhere else would
+    never reach it.
+
+    The hand-off is available only when the channel and planner modules
+    import and the installed vLLM carries the patch (its marker line in the
+    scheduler and the model runner).  Otherwise the connector declines such a
+    request (0 matched tokens): telling an unpatched vLLM that the filled
+    spans are matched would make it treat them as one contiguous prefix and
+    leave the gaps neither computed nor loaded.
+    """
+
+    PATCH_MARK = "# marathon: gapfill"
+    PATCHED_FILES = ("v1/core/sched/scheduler.py", "v1/worker/gpu_model_runner.py")
+
+    def __init__(self, channel: str = "marathon.gapfill_channel",
+                 planner: str = "marathon.gapfill", require_patch: bool = True) -> None:
+        self.channel_name, self.planner_name = channel, planner
+        self.require_patch = require_patch
+        self.channel = None
+        self.plan_gaps = None
+        self.why = ""
+        self._resolved = False
+
+    @classmethod
+    def vllm_patched(cls) -> bool:
+        """Whether the installed vLLM carries the gap-fill patch in both files."""
+        spec = importlib.util.find_spec("vllm")
+        if spec is None or not spec.submodule_search_locations:
+            return False
+        root = Path(next(iter(spec.submodule_search_locations)))
+        try:
+            return all(cls.PATCH_MARK in (root / f).read_text() for f in cls.PATCHED_FILES)
+        except OSError:
+            return False
+
+    def ready(self) -> bool:
+        """Resolve the channel, planner and patch once; True if the hand-off works."""
+        if not self._resolved:
+            self._resolved = True
+            try:
+                channel = importlib.import_module(self.channel_name)
+                planner = importlib.import_module(self.planner_name)
+                missing = [f for f in ("offer", "release") if not hasattr(channel, f)]
+                if missing or not hasattr(planner, "plan_gaps"):
+                    raise ImportError(f"{self.channel_name}/{self.planner_name} lack "
+                                      f"{missing or ['plan_gaps']}")
+            except ImportError as e:
+                self.why = f"gap-fill channel unavailable ({e})"
+                return False
+            if self.require_patch and not self.vllm_patched():
+                self.why = "the installed vLLM does not carry the gap-fill patch"
+                return False
+            self.channel, self.plan_gaps = channel, planner.plan_gaps
+        return self.channel is not None
+
+    def release(self, request_id: str) -> None:
+        if self.channel is not None:
+            self.channel.release(request_id)
+
+
 def _rope_theta(hf) -> float:
     theta = getattr(hf, "rope_theta", None)
     if theta is None:
@@ -197,6 +333,15 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         self._batch_save = bool(extra.get("batch_save", BATCH_SAVE))
         # loads from a store off the GPU overlap the forward pass, layer by layer
         self._async_tier = bool(extra.get("async_tier_load", True))
+        # a step's save status is read back when it is ready ("deferred": the
+        # forward pass is never stalled for it; it is waited for before any
+        # later load) or at the end of the step ("sync")
+        self._sync_save_check = str(extra.get("save_check", "deferred")) == "sync"
+        self._gapfill = bool(extra.get("gapfill", GAPFILL))
+        self._gap = GapHandoff(str(extra.get("gapfill_channel", "marathon.gapfill_channel")),
+                               str(extra.get("gapfill_planner", "marathon.gapfill")),
+                               bool(extra.get("gapfill_require_patch", True)))
+        self._gap_declined = False  # logged once
 
         # scheduler side
         self._table = SessionTable()
@@ -224,6 +369,18 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         self._head_size: int | None = None
         self._rope: RopeShift | None = None
         self._pending_saves: list[tuple[str, torch.Tensor]] = []
+        # save status: every save launch of a step ORs its rejected-token bits
+        # into one device word; its copy is read once ready
+        self._save_status: torch.Tensor | None = None
+        self._step_saves: list[_Save] | None = None  # saves issued this step
+        self._unchecked: list[tuple[torch.cuda.Event, torch.Tensor, list[_Save]]] = []
+        self._failed = ShiftWorkerMetadata()  # for the scheduler's mirror
+        self.save_failures = 0
+        # loads: the queued load's jobs (status read at wait_for_save) and the
+        # blocks of loads that did not land, for get_block_ids_with_load_errors
+        self._queued_jobs: list[LoadJob] = []
+        self._load_errors: set[int] = set()
+        self.verify_mismatches = 0
 
     # ---------------------------------------------------------------- scheduler
     def on_new_request(self, request: Request) -> None:
@@ -272,19 +429,25 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         params = self._params.get(request.request_id) or {}
 
         multi = params.get("loads")
-        if GAPFILL and session and multi and self._extents:
+        if self._gapfill and session and multi and self._extents:
             # a gap-filled step computes scattered positions; saving its range
             # as one generation would tag loaded keys as fresh ones
             logger.warning("shift: the extent store does not take single-request "
                            "multi-segment loads; recomputing")
             return 0, False
-        if GAPFILL and session and multi:
+        if self._gapfill and session and multi:
+            if not self._gap.ready():
+                # decline, never guess (vllm_shift_connector.py:104-109)
+                if not self._gap_declined:
+                    self._gap_declined = True
+                    logger.warning("shift: declining multi-segment reuse: %s", self._gap.why)
+                return 0, False
             accepted = self._accept_multi(request, session, multi, num_computed_tokens)
             if not accepted:
                 return 0, False
-            gp = gapfill.plan_gaps(accepted, self._bs, request.num_prompt_tokens,
-                                   local_hit=num_computed_tokens)
-            gapfill.offer(request.request_id, gp.compute, gp.filled_tokens)
+            gp = self._gap.plan_gaps(accepted, self._bs, request.num_prompt_tokens,
+                                     local_hit=num_computed_tokens)
+            self._gap.channel.offer(request.request_id, gp.compute, gp.filled_tokens)
             self._multi[request.request_id] = accepted
             logger.info("shift: gapfill %d segments, %d/%d tokens filled, %d to compute",
                         len(accepted), gp.filled_tokens, gp.n_prompt, len(gp.compute))
@@ -381,8 +544,20 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._forget(rid)
         return meta
 
+    def update_connector_output(self, connector_output) -> None:
+        """Scheduler side: apply the workers' failed saves to the mirror store."""
+        meta = getattr(connector_output, "kv_connector_worker_meta", None)
+        if isinstance(meta, ShiftWorkerMetadata):
+            self._apply_failed(meta)
+
+    def _apply_failed(self, meta: ShiftWorkerMetadata) -> None:
+        for session, pos in meta.truncate:
+            self._store.truncate(session, pos)
+        for session, gen, pos0, n in meta.release:
+            self._store.release(session, gen, pos0, n)
+
     def _forget(self, rid: str) -> None:
-        gapfill.release(rid)
+        self._gap.release(rid)
         self._multi.pop(rid, None)
         self._blocks.pop(rid, None)
         self._params.pop(rid, None)
@@ -412,6 +587,10 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._worker.layout = "split" if shape[0] == 2 else "split_blocks"
         else:
             raise AssertionError(f"expected a 4-D fused or 5-D split KV layout, got {shape}")
+        # an unsupported geometry fails here, at registration, as the
+        # reference's warmup did (vllm_shift_connector.py:405)
+        warmup(first, self._bs, bool(self._hnd), rotary=self._rotary,
+               layout=self._worker.layout, fp8=self._fp8)
         if first.is_cuda:
             self._worker.register(kv_caches)
         logger.info("marathon shift connector: %d layers, kv shape %s, layout %s, store %d tok",
@@ -449,12 +628,16 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                 if getattr(layer, "kv_cache", None) is not None
             }
             self.register_kv_caches(caches)
+        # a save of an earlier step that the kernel refused must be known (and
+        # its span forgotten) before any load reads those rows
+        self._poll_saves(block=True)
         if self._fp8:
             self._worker.k_scales = self._k_scales(forward_context)
             if self._worker.k_scales is not None:
                 self._worker.k_scales = self._worker.k_scales.to(self._worker.layers.device)
         if self._extents:
-            jobs = self._extent_load_jobs(meta.loads)
+            jobs, lost = self._extent_load_jobs(meta.loads)
+            self._note_load_errors(lost)
         else:
             jobs = [LoadJob(ld.session, ld.src_start, ld.delta, ld.dst_start, ld.length,
                             block_ids=ld.block_ids) for ld in meta.loads]
@@ -465,7 +648,16 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         # of it, without the host waiting for it as the reference did
         queued = self._async_tier and not VERIFY_LOAD
         t0 = time.perf_counter()
-        done = self._worker.load(jobs, check=True, asynchronous=queued)
+        try:
+            done = self._worker.load(jobs, check=True, asynchronous=queued)
+        except ShiftError as e:  # a synchronous load the kernel refused
+            logger.error("shift: load failed (%s); its blocks are reported for recompute", e)
+            self._note_load_errors(jobs)
+            return
+        # a job whose rows the store no longer holds stops the batch there
+        self._note_load_errors(jobs[len(done):])
+        if queued:
+            self._queued_jobs = list(done)
         ms = (time.perf_counter() - t0) * 1e3
         geo = self._worker.layers.geometry
         moved = sum(j.length for j in done) * len(self._worker.layers) * geo.heads * \
@@ -482,22 +674,43 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                         len(done), ms, moved / 2**20, moved / 2**30 / max(ms / 1e3, 1e-9))
         if VERIFY_LOAD and not self._extents:
             for j in done:
-                self._verify(j)
+                if not self._verify(j):
+                    self._note_load_errors([j])
         logger.info("shift: store %s", self._store.stats())
 
-    def _extent_load_jobs(self, loads: list[_Load]) -> list[LoadJob]:
-        """A load of generation ``gen``'s positions as one job per store extent."""
-        jobs = []
+    def _note_load_errors(self, jobs) -> None:
+        """Report the destination blocks of loads that did not land.
+
+        vLLM reads them through ``get_block_ids_with_load_errors`` and
+        recomputes those blocks (or fails the request, per its
+        ``kv_load_failure_policy``) instead of attending to stale KV.
+        """
+        for j in jobs:
+            if j.block_ids is None or j.length <= 0:
+                continue
+            lo = j.dst_start // self._bs
+            hi = -(-(j.dst_start + j.length) // self._bs)
+            self._load_errors.update(int(b) for b in list(j.block_ids)[lo:hi])
+
+    def get_block_ids_with_load_errors(self) -> set[int]:
+        out, self._load_errors = self._load_errors, set()
+        return out
+
+    def _extent_load_jobs(self, loads: list[_Load]) -> tuple[list[LoadJob], list[_Load]]:
+        """A load of generation ``gen``'s positions as one job per store extent,
+        plus the loads whose rows the store no longer holds."""
+        jobs, lost = [], []
         for ld in loads:
             where = self._store.locate(ld.session, ld.gen, ld.src_start, ld.length, count=False)
             if where is None:
                 logger.error("shift: session %s generation %d lost [%d,%d); load skipped",
                              ld.session, ld.gen, ld.src_start, ld.src_start + ld.length)
+                lost.append(ld)
                 continue
             for p0, n, row in where:
                 jobs.append(LoadJob(ld.session, p0, ld.delta, p0 + ld.delta, n,
                                     block_ids=ld.block_ids, store_start=row))
-        return jobs
+        return jobs, lost
 
     def _extent_save_jobs(self, save: _Save) -> list[SaveJob]:
         """This step's fresh positions as one job per extent (the scheduler's allocation)."""
@@ -505,37 +718,62 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                 for p0, n, row in self._store.save_extent(save.session, save.gen,
                                                          save.dst_start, save.length)]
 
-    def _verify(self, job: LoadJob) -> None:
-        """Read a loaded span back and compare it with a torch fp32 re-rotation."""
-        if self._rotary != self._head_size:
-            logger.warning("shift-verify: partial rotary (%d of %d) unsupported; skipped",
-                           self._rotary, self._head_size)
-            return
+    def _verify(self, job: LoadJob) -> bool:
+        """Read a loaded span back and check it against the torch fp32 rotation.
+
+        The reference's diagnostic (``vllm_shift_connector.py:444-479``) with a
+        pass/fail bar instead of a logged difference: V and any non-rotary
+        tail bit for bit, and every rotated K element within one unit in the
+        last place (of the cache dtype) of ``k*cos + rotate_half(k)*sin``
+        evaluated in fp32 with torch's fp32 cos/sin of ``fp32(delta) *
+        inv_freq`` -- the reference's own tables (``shift_kernels.py:68-84``).
+        It runs on the host, on copies of the store rows and of the paged
+        rows, so it shares nothing with the kernel.  Returns False (and logs
+        an error) on any mismatch.
+        """
         geo = self._worker.layers.geometry
-        d = geo.head_size
+        cache_dtype = self._worker.layers.tensors[0].dtype
+        if cache_dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            logger.warning("shift-verify: %s cache unsupported; skipped", cache_dtype)
+            return True
+        d, rot = geo.head_size, self._rotary
+        h = rot // 2
+        ang = float(job.delta) * self._inv_freq.to(torch.float32)
+        cos, sin = torch.cat((ang, ang)).cos(), torch.cat((ang, ang)).sin()
         sl = job.host_slots(self._bs)
+        blk, off = sl // self._bs, sl % self._bs
+        bits = {2: torch.int16, 4: torch.int32}[geo.elem_bytes]
+        ok = True
         for name, kv in zip(self._worker.layers.names, self._worker.layers.tensors, strict=True):
-            row = self._store.read(job.session, name, job.src_start, job.length)
+            row = self._store.read(job.session, name, job.row, job.length)
             if row is None:
                 continue
-            row = row.to(kv.device)  # a host or peer store tier
-            sh = self._shift(job.delta, kv.device)
-            kf = row[..., :d].float()
-            h = d // 2
-            want_k = kf * sh.emb_cos + torch.cat((-kf[..., h:], kf[..., :h]), -1) * sh.emb_sin
-            blk, off = (sl // self._bs).to(kv.device), (sl % self._bs).to(kv.device)
+            row = row.cpu()
+            b, o = blk.to(kv.device), off.to(kv.device)
             if geo.kind == "hnd":
-                got = kv[blk, :, off]
+                got = kv[b, :, o]
             elif geo.kind == "nhd":
-                got = kv[blk, off]
+                got = kv[b, o]
             else:
                 kk, vv = (kv[0], kv[1]) if geo.kind == "split" else (kv[:, 0], kv[:, 1])
-                got = torch.cat((kk[blk, off], vv[blk, off]), -1)
-            want = torch.cat((want_k, row[..., d:].float()), -1)
-            diff = (got.float() - want).abs()
-            logger.info("shift-verify: layer=%s delta=%d n=%d max_abs=%.4g max_rel=%.4g", name,
-                        job.delta, job.length, float(diff.max()),
-                        float(diff.max() / want.abs().max().clamp_min(1e-6)))
+                got = torch.cat((kk[b, o], vv[b, o]), -1)
+            got = got.cpu()
+            kf = row[..., :rot].float()
+            want = kf * cos + torch.cat((-kf[..., h:], kf[..., :h]), -1) * sin
+            k_off = (got[..., :rot].float() - want).abs() > ulp(want, cache_dtype)
+            exact = got[..., rot:].view(bits) != row[..., rot:].view(bits)
+            n_k, n_x = int(k_off.sum()), int(exact.sum())
+            if n_k or n_x:
+                ok = False
+                logger.error("shift-verify: layer=%s delta=%d n=%d: %d K elements beyond one "
+                             "ulp of the fp32 rotation, %d V/tail elements not bit-equal",
+                             name, job.delta, job.length, n_k, n_x)
+            else:
+                logger.info("shift-verify: layer=%s delta=%d n=%d ok", name, job.delta,
+                            job.length)
+        if not ok:
+            self.verify_mismatches += 1
+        return ok
 
     def wait_for_layer_load(self, layer_name: str) -> None:
         if self._worker.pending is not None and layer_name in self._worker.layers.index:
@@ -559,12 +797,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         self._save_layers([layer_name], meta)
 
     def _save_layers(self, names: list[str], meta: ShiftConnectorMetadata) -> None:
-        jobs = []
+        jobs, issued = [], []
         if self._extents:
             for save in meta.saves:
                 jobs.extend(self._extent_save_jobs(save))
-            if jobs:
-                self._worker.save(jobs, names, check=False)
+                issued.append(save)
+            self._issue_saves(jobs, names, issued)
             return
         for save in meta.saves:
             # mirrors the scheduler's reserve for this step; idempotent across layers
@@ -572,38 +810,90 @@ class MarathonShiftConnector(KVConnectorBase_V1):
                 continue
             jobs.append(SaveJob(save.session, save.dst_start, save.length,
                                 block_ids=save.block_ids))
-        if jobs:
-            self._worker.save(jobs, names, check=False)
+            issued.append(save)
+        self._issue_saves(jobs, names, issued)
+
+    def _issue_saves(self, jobs: list[SaveJob], names: list[str], saves: list[_Save]) -> None:
+        """Launch a save; its rejected-token bits join the step's status word."""
+        if not jobs:
+            return
+        if self._step_saves is None:  # the step's first save: a fresh status word
+            if self._save_status is None:
+                self._save_status = torch.zeros(4, dtype=torch.int32,
+                                                device=self._worker.layers.device)
+            else:
+                self._save_status.zero_()
+            self._step_saves = list(saves)
+        self._worker.save(jobs, names, check=False, err=self._save_status.data_ptr())
 
     def wait_for_save(self):
-        self._worker.finish_pending()  # this step's queued load: wait, check its status
-        if not self._pending_saves:
-            return
-        meta = self._get_connector_metadata() if self.has_connector_metadata() else None
-        names = [n for n, _ in self._pending_saves]
-        self._pending_saves = []
-        if not isinstance(meta, ShiftConnectorMetadata) or not meta.saves:
-            return
-        # one launch per run of consecutive layers (normally: all of them)
-        order = sorted(names, key=self._worker.layers.index.__getitem__)
-        group: list[str] = []
-        for n in order:
-            if group and self._worker.layers.index[n] != self._worker.layers.index[group[-1]] + 1:
-                self._save_layers_batched(group, meta)
-                group = []
-            group.append(n)
-        if group:
-            self._save_layers_batched(group, meta)
+        # this step's queued load: the stream waits for it, the host reads its status
+        try:
+            self._worker.finish_pending()
+        except ShiftError as e:
+            logger.error("shift: load failed (%s); its blocks are reported for recompute", e)
+            self._note_load_errors(self._queued_jobs)
+        self._queued_jobs = []
+        if self._pending_saves:
+            meta = self._get_connector_metadata() if self.has_connector_metadata() else None
+            names = [n for n, _ in self._pending_saves]
+            self._pending_saves = []
+            if isinstance(meta, ShiftConnectorMetadata) and meta.saves:
+                # one launch per run of consecutive layers (normally: all of them)
+                order = sorted(names, key=self._worker.layers.index.__getitem__)
+                group: list[str] = []
+                for n in order:
+                    if group and self._worker.layers.index[n] != \
+                            self._worker.layers.index[group[-1]] + 1:
+                        self._save_layers(group, meta)
+                        group = []
+                    group.append(n)
+                if group:
+                    self._save_layers(group, meta)
+        self._close_step_saves()
 
-    def _save_layers_batched(self, names: list[str], meta: ShiftConnectorMetadata) -> None:
-        if self._extents:
-            self._save_layers(names, meta)
+    def _close_step_saves(self) -> None:
+        """Queue the read-back of this step's save status (read when it is ready)."""
+        if self._step_saves is None:
             return
-        jobs = []
-        for save in meta.saves:
-            if not self._store.reserve(save.session, save.dst_start, save.length):
-                continue
-            jobs.append(SaveJob(save.session, save.dst_start, save.length,
-                                block_ids=save.block_ids))
-        if jobs:
-            self._worker.save(jobs, names, check=False)
+        word = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        word.copy_(self._save_status[:1], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._unchecked.append((ev, word, self._step_saves))
+        self._step_saves = None
+        self._poll_saves(block=self._sync_save_check)
+
+    def _poll_saves(self, block: bool) -> None:
+        """Read the save statuses that are ready (all of them when ``block``)."""
+        while self._unchecked:
+            ev, word, saves = self._unchecked[0]
+            if not block and not ev.query():
+                return
+            ev.synchronize()
+            self._unchecked.pop(0)
+            bits = int(word[0])
+            if bits:
+                self._saves_failed(saves, bits)
+
+    def _saves_failed(self, saves: list[_Save], bits: int) -> None:
+        """Forget the spans of a refused save here and, through the worker
+        metadata, in the scheduler's mirror: the next turn recomputes them."""
+        self.save_failures += 1
+        logger.error("shift: the save kernel rejected tokens (%s); dropping %d stored span(s) "
+                     "so later turns recompute them", _lib.describe_bits(bits), len(saves))
+        for sv in saves:
+            if self._extents:
+                self._store.release(sv.session, sv.gen, sv.dst_start, sv.length)
+                self._failed.release.append((sv.session, sv.gen, sv.dst_start, sv.length))
+            else:
+                self._store.truncate(sv.session, sv.dst_start)
+                self._failed.truncate.append((sv.session, sv.dst_start))
+
+    def build_connector_worker_meta(self):
+        """Failed saves for the scheduler's mirror (None when there are none)."""
+        self._poll_saves(block=False)
+        if not self._failed:
+            return None
+        out, self._failed = self._failed, ShiftWorkerMetadata()
+        return out

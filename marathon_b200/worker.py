@@ -213,12 +213,15 @@ class ShiftWorker:
 
     # ---------------------------------------------------------------- save
     def save(self, jobs: list[SaveJob], layer_names: list[str] | None = None, *,
-             check: bool = True) -> int:
+             check: bool = True, err: int | None = None) -> int:
         """Gather ``jobs`` out of the paged caches of ``layer_names`` into the store.
 
         The layers must be consecutive in registration order (one launch covers
         a contiguous range); the store rows must already be reserved.  Returns
-        the number of token-layers written.
+        the number of token-layers written.  ``check`` waits and raises on
+        rejected tokens; ``err`` (a device address, with ``check=False``) makes
+        the kernels OR their rejected-token bits into that word instead, for a
+        caller that reads one status per step.
         """
         if not jobs:
             return 0
@@ -250,7 +253,7 @@ class ShiftWorker:
             return 0
         view = self.store.view(list(rows), names)
         mover = self.mover or self.launcher
-        mover.save(runs, view, first_layer=first, n_layers=len(names), check=check)
+        mover.save(runs, view, first_layer=first, n_layers=len(names), check=check, err=err)
         done = sum(r.length for r in runs)
         self.store.mark_saved(done, len(names))
         return done * len(names)

@@ -16,35 +16,8 @@ import torch
 vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.base")
 KVConnectorRole = vllm_base.KVConnectorRole
 
-from marathon_b200 import gapfill  # noqa: E402
 from marathon_b200 import vllm_shift_connector as C  # noqa: E402
-
-BS = 16
-
-
-def fake_config(extra=None, head_dim=128, cache_dtype="auto"):
-    hf = SimpleNamespace(head_dim=head_dim, hidden_size=4096, num_attention_heads=32,
-                         partial_rotary_factor=1.0, rope_theta=1e6)
-    return SimpleNamespace(
-        kv_transfer_config=SimpleNamespace(kv_connector_extra_config=extra or {}),
-        cache_config=SimpleNamespace(block_size=BS, cache_dtype=cache_dtype),
-        model_config=SimpleNamespace(hf_text_config=hf),
-    )
-
-
-def request(rid, params, n_prompt):
-    return SimpleNamespace(request_id=rid, kv_transfer_params=params, num_prompt_tokens=n_prompt)
-
-
-def new_req(rid, blocks, computed):
-    return SimpleNamespace(req_id=rid, block_ids=(list(blocks),), num_computed_tokens=computed)
-
-
-def sched_output(new=(), cached=None, scheduled=None, finished=()):
-    cached = cached or SimpleNamespace(req_ids=[], new_block_ids=[], num_computed_tokens=[])
-    return SimpleNamespace(scheduled_new_reqs=list(new), scheduled_cached_reqs=cached,
-                           num_scheduled_tokens=dict(scheduled or {}),
-                           finished_req_ids=set(finished))
+from vllm_fakes import BS, fake_config, forward_context, new_req, request, sched_output  # noqa: E402,E501
 
 
 def scheduler(extra=None):
@@ -166,30 +139,6 @@ def test_second_in_flight_writer_on_a_session_is_refused():
     meta = conn.build_connector_meta(sched_output([new_req("b", [1, 2, 3, 4, 5, 6, 7], 0)],
                                                   scheduled={"b": 100}))
     assert meta.saves == []  # no session -> pass-through, no save
-
-
-def test_gapfill_accepts_multiple_segments(monkeypatch):
-    monkeypatch.setattr(C, "GAPFILL", True)
-    gapfill.clear()
-    conn = scheduler()
-    conn._store.reserve("s", 0, 2000)
-    loads = [{"dst_start": 100, "dst_end": 600, "delta": 20},
-             {"dst_start": 700, "dst_end": 1500, "delta": -40},
-             {"dst_start": 1600, "dst_end": 1605, "delta": 3}]  # under a block: dropped
-    r = request("g", {"session": "s", "loads": loads, "save": "full"}, 2000)
-    conn.on_new_request(r)
-    n, _ = conn.get_num_new_matched_tokens(r, 0)
-    accepted = conn._multi["g"]
-    assert [(a["dst_start"], a["dst_end"]) for a in accepted] == [(112, 592), (704, 1488)]
-    assert n == (592 - 112) + (1488 - 704)
-    assert "g" in gapfill._offered
-    conn.update_state_after_alloc(r, None, n)
-    meta = conn.build_connector_meta(sched_output([new_req("g", range(200), 0)],
-                                                  scheduled={"g": 2000 - n}))
-    assert [(ld.src_start, ld.delta, ld.length) for ld in meta.loads] == [
-        (92, 20, 480), (744, -40, 784)]
-    conn.request_finished(r, [])
-    assert "g" not in gapfill._offered
 
 
 def test_stats_merges_instances():
@@ -369,9 +318,203 @@ def test_extent_mode_worker_splits_loads_and_saves_by_extent():
     st.save_extent("s", 0, 0, 100)
     st.save_extent("s", 1, 0, 50)  # another generation takes the next rows
     st.save_extent("s", 0, 100, 60)  # generation 0 continues elsewhere
-    jobs = conn._extent_load_jobs([C._Load("s", 40, 12, 52, 100, [0, 1, 2], BS, 0)])
+    jobs, lost = conn._extent_load_jobs([C._Load("s", 40, 12, 52, 100, [0, 1, 2], BS, 0)])
     assert [(j.src_start, j.length, j.store_start, j.dst_start, j.delta) for j in jobs] == \
-        [(40, 60, 40, 52, 12), (100, 40, 150, 112, 12)]
+        [(40, 60, 40, 52, 12), (100, 40, 150, 112, 12)] and lost == []
     saves = conn._extent_save_jobs(C._Save("s", 160, 30, [0, 1, 2], BS, 0))
     assert [(j.dst_start, j.length, j.store_start) for j in saves] == [(160, 30, 210)]
-    assert conn._extent_load_jobs([C._Load("s", 0, 0, 0, 10, [0], BS, 7)]) == []  # unknown gen
+    unknown = C._Load("s", 0, 0, 0, 10, [0], BS, 7)  # a generation the store never held
+    assert conn._extent_load_jobs([unknown]) == ([], [unknown])
+
+
+# ------------------------------------------------- failures: decline, never guess
+def test_failed_save_is_forgotten_by_worker_and_scheduler_mirror():
+    """A save the kernel refused truncates the session on the worker; the worker
+    metadata carries the truncation to the scheduler's mirror, whose next plan
+    declines the span instead of loading rows that were never written."""
+    sched = scheduler()
+    worker = C.MarathonShiftConnector(fake_config({"store_tokens": 65536, "store_device": "cpu"}),
+                                      KVConnectorRole.WORKER, None)
+    for st in (sched._store, worker._store):
+        assert st.reserve("s", 0, 600)
+    save = C._Save("s", 0, 600, list(range(40)), BS)
+    worker._saves_failed([save], 1)  # the step's status word had MSHIFT_EBIT_SLOT
+    assert worker.save_failures == 1 and not worker._store.covers("s", 64, 16)
+    wmeta = worker.build_connector_worker_meta()
+    assert isinstance(wmeta, C.ShiftWorkerMetadata) and wmeta.truncate == [("s", 0)]
+    assert worker.build_connector_worker_meta() is None  # reported once
+    sched.update_connector_output(SimpleNamespace(kv_connector_worker_meta=wmeta))
+    r = request("r1", {"session": "s", "load": {"dst_start": 64, "dst_end": 600, "delta": 8}},
+                700)
+    sched.on_new_request(r)
+    assert sched.get_num_new_matched_tokens(r, 64) == (0, False)
+    # a later save that would leave a hole above the truncation is refused on both sides
+    assert not sched._store.reserve("s", 600, 10) and not worker._store.reserve("s", 600, 10)
+
+
+def test_worker_metadata_aggregates_ranks():
+    a = C.ShiftWorkerMetadata(truncate=[("s", 0)])
+    b = C.ShiftWorkerMetadata(release=[("t", 1, 0, 16)])
+    ab = a.aggregate(b)
+    assert ab.truncate == [("s", 0)] and ab.release == [("t", 1, 0, 16)] and ab
+    assert not C.ShiftWorkerMetadata()
+
+
+def test_failed_extent_save_releases_that_generation():
+    sched = scheduler({"store_tokens": 8192, "store_mode": "extents"})
+    worker = C.MarathonShiftConnector(fake_config({"store_tokens": 8192, "store_mode": "extents",
+                                                   "store_device": "cpu"}),
+                                      KVConnectorRole.WORKER, None)
+    for st in (sched._store, worker._store):
+        assert st.save_extent("s", 0, 0, 300)
+    worker._saves_failed([C._Save("s", 0, 300, list(range(19)), BS, 0)], 2)
+    wmeta = worker.build_connector_worker_meta()
+    assert wmeta.release == [("s", 0, 0, 300)]
+    sched.update_connector_output(SimpleNamespace(kv_connector_worker_meta=wmeta))
+    for st in (sched._store, worker._store):
+        assert st.locate("s", 0, 0, 300, count=False) is None
+
+
+def test_load_errors_name_the_destination_blocks():
+    from marathon_b200.worker import LoadJob
+
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192, "store_device": "cpu"}),
+                                    KVConnectorRole.WORKER, None)
+    table = list(range(100, 140))
+    conn._note_load_errors([LoadJob("s", 0, 0, 32, 48, block_ids=table),  # blocks 2..4
+                            LoadJob("s", 0, 0, 100, 1, block_ids=table)])  # block 6
+    assert conn.get_block_ids_with_load_errors() == {102, 103, 104, 106}
+    assert conn.get_block_ids_with_load_errors() == set()
+
+
+def test_registration_runs_warmup(monkeypatch):
+    seen = []
+    monkeypatch.setattr(C, "warmup", lambda kv, bs, hnd, **kw: seen.append((bs, hnd, kw)))
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192}),
+                                    KVConnectorRole.WORKER, None)
+    conn.register_kv_caches({"l0": torch.zeros(4, BS, 2, 256, dtype=torch.bfloat16)})
+    assert seen == [(BS, False, {"rotary": 128, "layout": "nhd", "fp8": False})]
+
+
+def test_ulp_matches_the_dtype_spacing():
+    x = torch.tensor([1.0, 1.5, 2.0, 3.0, -0.75, 0.0, 1e-40, 2.0**-126], dtype=torch.float32)
+    want = [2.0**-7, 2.0**-7, 2.0**-6, 2.0**-6, 2.0**-8, 2.0**-133, 2.0**-133, 2.0**-133]
+    assert C.ulp(x, torch.bfloat16).tolist() == want
+    assert C.ulp(torch.tensor([1.0]), torch.float16).tolist() == [2.0**-10]
+    # the next bf16 value above x is exactly one ulp away
+    for v in (1.0, 3.0, 1000.0, 2.0**-120):
+        t = torch.tensor([v], dtype=torch.bfloat16)
+        nxt = t.view(torch.int16) + 1
+        assert float(nxt.view(torch.bfloat16)) - v == float(C.ulp(t.float(), torch.bfloat16))
+
+
+def _worker_with_caches(cuda, extra=None, L=3, NBLK=96, H=8, D=128, seed=7):
+    cfg = {"store_tokens": 8192, **(extra or {})}
+    conn = C.MarathonShiftConnector(fake_config(cfg), KVConnectorRole.WORKER, None)
+    g = torch.Generator().manual_seed(seed)
+    caches = {f"model.layers.{i}.self_attn.attn":
+              torch.randn(NBLK, BS, H, 2 * D, generator=g).to(torch.bfloat16).to(cuda)
+              for i in range(L)}
+    conn.register_kv_caches(caches)
+    return conn, caches
+
+
+def _save_step(conn, caches, saves):
+    conn.bind_connector_metadata(C.ShiftConnectorMetadata(saves=saves))
+    for name, kv in caches.items():
+        conn.save_kv_layer(name, kv, None)
+    conn.wait_for_save()
+    conn.clear_connector_metadata()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch_save", [False, True])
+def test_refused_save_makes_the_next_edit_turn_recompute(cuda, batch_save):
+    """A save whose block table holds an out-of-range block id: the kernel skips
+    those tokens and flags them; the session is truncated on the worker and,
+    through the worker metadata, in the scheduler's mirror, so the next edit
+    turn recomputes instead of loading the stale rows.  The control run with a
+    valid table loads."""
+    outcomes = {}
+    for bad in (False, True):
+        sched = scheduler({"store_tokens": 8192})
+        conn, caches = _worker_with_caches(cuda, {"batch_save": batch_save})
+        r0 = request("r0", {"session": "s", "save": True}, 600)
+        sched.on_new_request(r0)
+        assert sched.get_num_new_matched_tokens(r0, 0) == (0, False)
+        blocks0 = list(range(40))
+        if bad:
+            blocks0[20] = 96 + 5  # past the last block of the cache
+        meta = sched.build_connector_meta(sched_output([new_req("r0", blocks0, 0)],
+                                                       scheduled={"r0": 600}))
+        sched.request_finished(r0, blocks0)
+        conn._store.reserve("s", 0, 600)  # the worker mirrors the scheduler's reserve
+        _save_step(conn, caches, meta.saves)
+        torch.cuda.synchronize()
+        wmeta = conn.build_connector_worker_meta()
+        sched.update_connector_output(SimpleNamespace(kv_connector_worker_meta=wmeta))
+        r1 = request("r1", {"session": "s", "load": {"dst_start": 64, "dst_end": 600,
+                                                     "delta": 24}}, 700)
+        sched.on_new_request(r1)
+        outcomes[bad] = (sched.get_num_new_matched_tokens(r1, 64)[0], conn.save_failures,
+                         wmeta)
+    n_ok, fails_ok, meta_ok = outcomes[False]
+    n_bad, fails_bad, meta_bad = outcomes[True]
+    assert n_ok == 592 - 64 and fails_ok == 0 and meta_ok is None
+    assert n_bad == 0 and fails_bad == 1 and meta_bad.truncate == [("s", 0)]
+
+
+@pytest.mark.gpu
+def test_refused_load_reports_its_blocks(cuda):
+    """A queued load whose block table points past the cache: the status read at
+    wait_for_save names the load's destination blocks for vLLM to recompute."""
+    conn, caches = _worker_with_caches(cuda)
+    assert conn._store.reserve("s", 0, 600)
+    _save_step(conn, caches, [C._Save("s", 0, 600, list(range(40)), BS)])
+    bt = list(range(40, 80))
+    bt[10] = 96 + 1
+    conn.bind_connector_metadata(C.ShiftConnectorMetadata(
+        loads=[C._Load("s", 64, 16, 80, 512, bt, BS)]))
+    conn.start_load_kv(forward_context())
+    conn.wait_for_save()
+    conn.clear_connector_metadata()
+    assert conn.get_block_ids_with_load_errors() == set(bt[80 // BS : (80 + 512) // BS])
+
+
+@pytest.mark.gpu
+def test_verify_load_passes_a_correct_load_and_reports_a_planted_mismatch(cuda, monkeypatch):
+    """``MARATHON_VERIFY_LOAD``: every loaded layer is read back and held to the
+    north-star bar against torch's fp32 rotation with the reference's tables.
+    A correct load passes.  Then the mistake is planted in the checker's own
+    input on the CPU (the inverse frequencies it rotates with are perturbed),
+    and the check must report the mismatch and the load's blocks."""
+    monkeypatch.setattr(C, "VERIFY_LOAD", True)
+    conn, caches = _worker_with_caches(cuda)
+    assert conn._store.reserve("s", 0, 600)
+    _save_step(conn, caches, [C._Save("s", 0, 600, list(range(40)), BS)])
+    bt = list(range(40, 80))
+
+    def load(delta):
+        conn.bind_connector_metadata(C.ShiftConnectorMetadata(
+            loads=[C._Load("s", 64, delta, 64 + delta, 512, bt, BS)]))
+        conn.start_load_kv(forward_context())
+        conn.wait_for_save()
+        conn.clear_connector_metadata()
+
+    load(16)
+    assert conn.verify_mismatches == 0 and conn.get_block_ids_with_load_errors() == set()
+    monkeypatch.setattr(conn, "_inv_freq", conn._inv_freq * 1.001)
+    load(32)
+    assert conn.verify_mismatches == 1
+    assert conn.get_block_ids_with_load_errors() == set(bt[96 // BS : (96 + 512) // BS])
+
+
+@pytest.mark.gpu
+def test_registration_rejects_a_geometry_no_kernel_serves(cuda):
+    conn = C.MarathonShiftConnector(fake_config({"store_tokens": 8192}, head_dim=96),
+                                    KVConnectorRole.WORKER, None)
+    from marathon_b200.shift_kernels import ShiftError
+
+    with pytest.raises(ShiftError, match="no kernel"):
+        conn.register_kv_caches({"l0": torch.zeros(8, BS, 2, 192, dtype=torch.bfloat16,
+                                                   device=cuda)})

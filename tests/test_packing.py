@@ -34,6 +34,9 @@ class _FakeStaging:
     def upload(self, slot: int, n: int, stream_ptr: int) -> None:
         self.total = n
 
+    def finish(self, slot: int, stream) -> None:
+        self.finished = slot
+
 
 class _FakeSlots:
     """Stands in for a CUDA int64 slot tensor (only its address is packed)."""

@@ -49,7 +49,8 @@ def _runs(tables_of_runs, bt_ptr, bt_len):
     return rec, tiles
 
 
-def test_noalloc_load_matches_the_allocating_entry_points(cuda):
+@pytest.mark.parametrize("rotary", [128, 64], ids=["full-rotary", "partial-rotary"])
+def test_noalloc_load_matches_the_allocating_entry_points(cuda, rotary):
     lib = _lib.load()
     g = torch.Generator().manual_seed(21)
     stores = [[torch.randn(400, H, 2 * D, generator=g).to(torch.bfloat16).to(cuda)
@@ -66,7 +67,8 @@ def test_noalloc_load_matches_the_allocating_entry_points(cuda):
     v_ref = k_ref + D * 2
     k_new = torch.tensor([t.data_ptr() for t in kv_new], dtype=torch.int64, device=cuda)
     v_new = k_new + D * 2
-    inv = inv_freq(D, 1e6).to(cuda)
+    inv = inv_freq(rotary, 1e6).to(cuda)
+    half = rotary // 2
     err = torch.zeros(2, dtype=torch.int32, device=cuda)
     paged = _lib.Paged(BS * H * 2 * D, H * 2 * D, 2 * D, NBLK, BS, H, D, _lib.BF16)
     stream = torch.cuda.current_stream(cuda).cuda_stream
@@ -78,14 +80,14 @@ def test_noalloc_load_matches_the_allocating_entry_points(cuda):
         rec, tiles = _runs(which, bt.data_ptr(), bt.numel())
         runs = torch.from_numpy(rec.view(np.uint8).copy()).to(cuda)
 
-        tables = torch.empty(len(deltas), 2, D // 2, dtype=torch.float32, device=cuda)
-        _lib.check(lib.mshift_rope_tables(d.data_ptr(), len(deltas), inv.data_ptr(), D // 2,
+        tables = torch.empty(len(deltas), 2, half, dtype=torch.float32, device=cuda)
+        _lib.check(lib.mshift_rope_tables(d.data_ptr(), len(deltas), inv.data_ptr(), half,
                                           tables.data_ptr(), stream), "tables")
-        _lib.check(lib.mshift_load(paged, D, runs.data_ptr(), len(rec), 32, tiles, L,
+        _lib.check(lib.mshift_load(paged, rotary, runs.data_ptr(), len(rec), 32, tiles, L,
                                    store_ptrs.data_ptr(), caps.data_ptr(), 2, H * 2 * D, 2 * D,
                                    k_ref.data_ptr(), v_ref.data_ptr(), tables.data_ptr(),
                                    len(deltas), None, err.data_ptr(), stream), "load")
-        _lib.check(lib.mshift_load_noalloc(paged, D, runs.data_ptr(), len(rec), 32, tiles, L,
+        _lib.check(lib.mshift_load_noalloc(paged, rotary, runs.data_ptr(), len(rec), 32, tiles, L,
                                            store_ptrs.data_ptr(), caps.data_ptr(), 2, H * 2 * D,
                                            2 * D, k_new.data_ptr(), v_new.data_ptr(),
                                            d.data_ptr(), len(deltas), inv.data_ptr(), None,
@@ -112,5 +114,22 @@ def test_noalloc_rejects_more_deltas_than_its_scratch_holds(cuda):
                                  torch.cuda.current_stream(cuda).cuda_stream)
     assert rc == _lib.ETOOBIG
     assert b"static scratch" in lib.mshift_strerror(rc)
+    torch.cuda.synchronize()
+    assert torch.equal(kv, before)
+
+
+def test_noalloc_rejects_a_rotary_wider_than_its_scratch_rows(cuda):
+    """Scratch rows hold rotary/2 <= 128 frequencies: rotary 258 is refused
+    with MSHIFT_ETOOBIG before anything is launched, and the cache is unchanged."""
+    lib = _lib.load()
+    kv = torch.zeros(NBLK, BS, H, 2 * D, dtype=torch.bfloat16, device=cuda)
+    before = kv.clone()
+    paged = _lib.Paged(BS * H * 2 * D, H * 2 * D, 2 * D, NBLK, BS, H, D, _lib.BF16)
+    d = torch.zeros(1, dtype=torch.int64, device=cuda)
+    p = ctypes.c_void_p(kv.data_ptr())
+    rc = lib.mshift_load_noalloc(paged, 258, p, 1, 32, 1, 1, p, p, 1, H * 2 * D, 2 * D, p, p,
+                                 d.data_ptr(), 1, p, None, p,
+                                 torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == _lib.ETOOBIG
     torch.cuda.synchronize()
     assert torch.equal(kv, before)
