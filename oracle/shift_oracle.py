@@ -80,14 +80,46 @@ def _e4m3_magnitudes() -> np.ndarray:
 _E4M3 = _e4m3_magnitudes()
 
 
+def _e4m3_values() -> np.ndarray:
+    """fp32 value of every code 0..255 (0x7F, 0xFF: NaN)."""
+    mag = np.append(_E4M3, np.nan).astype(np.float32)
+    return np.concatenate((mag, -mag)).astype(np.float32)
+
+
+_E4M3_F32 = _e4m3_values()
+
+
 def e4m3_to_f32(codes: np.ndarray) -> np.ndarray:
-    c = np.asarray(codes, dtype=np.uint8).astype(np.int64)
-    mag = np.where((c & 0x7F) == 0x7F, np.nan, _E4M3[np.minimum(c & 0x7F, 126)])
-    return np.where(c & 0x80, -mag, mag).astype(np.float32)
+    return _E4M3_F32[np.asarray(codes, dtype=np.uint8)]
 
 
 def f32_to_e4m3(x: np.ndarray) -> np.ndarray:
-    """Saturate to +-448 then round to the nearest e4m3fn code, ties to even."""
+    """Saturate to +-448 then round to the nearest e4m3fn code, ties to even.
+
+    Integer arithmetic on the fp32 bit pattern: at or above 2**-6 (e4m3's
+    smallest normal) the 24-bit significand is rounded to 4 bits (hidden bit
+    plus 3), carrying into the exponent on overflow; below it the value is a
+    multiple of 2**-9 and ``rint(|x| * 2**9)`` (exact scaling, ties to even) is
+    the code.  Pinned against torch's own conversion by the golden vectors.
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    a = np.minimum(np.abs(x), np.float32(E4M3_MAX))
+    u = a.view(np.int32)
+    e = (u >> 23) - 127  # unbiased exponent of a normal fp32
+    sig = (u & 0x7FFFFF) | 0x800000
+    q = sig >> 20
+    rem = sig & 0xFFFFF
+    q += (rem > 0x80000) | ((rem == 0x80000) & ((q & 1) == 1))
+    carry = q >> 4  # 1.111 rounded up to 10.000
+    normal = ((e + carry + 7) << 3) | ((q >> carry) & 7)
+    sub = np.rint(a * np.float32(2.0**9)).astype(np.int32)  # exact scaling below 2**-6
+    code = np.where(a >= np.float32(2.0**-6), normal, sub).astype(np.uint8)
+    code = np.where(np.signbit(x), code | np.uint8(0x80), code).astype(np.uint8)
+    return np.where(np.isnan(x), np.uint8(0x7F), code)
+
+
+def _f32_to_e4m3_by_search(x: np.ndarray) -> np.ndarray:
+    """Nearest code by search over the 127 magnitudes (the definition; slow)."""
     x = np.asarray(x, dtype=np.float32)
     neg = np.signbit(x)
     a = np.minimum(np.abs(x).astype(np.float64), E4M3_MAX)
@@ -303,3 +335,32 @@ def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray, dtype: str) -> np.ndarr
         return np.where(u & 0x80000000, 0x80000000 - u, u)
 
     return np.abs(ordered(a_bits) - ordered(b_bits))
+
+
+# ------------------------------------------------------------ tolerance bar
+#: stored mantissa bits and smallest normal exponent of each cache format
+_FORMAT = {BF16: (7, -126), F16: (10, -14), F32: (23, -126), E4M3: (3, -6)}
+
+
+def ulp_of(r: np.ndarray, dtype: str) -> np.ndarray:
+    """Spacing of ``dtype`` at each real value ``r``: ``2**(e - m)`` for ``|r|`` in
+    ``[2**e, 2**(e+1))`` with ``m`` stored mantissa bits, the subnormal spacing
+    below the smallest normal binade.  E4M3 values are taken after saturation."""
+    m, emin = _FORMAT[dtype]
+    a = np.abs(np.asarray(r, dtype=np.float64))
+    if dtype == E4M3:
+        a = np.minimum(a, E4M3_MAX)
+    _, e = np.frexp(a)  # a = f * 2**e, 0.5 <= f < 1 (e = 0 at a = 0)
+    e = np.where(a > 0, e - 1, emin)
+    return np.ldexp(1.0, np.maximum(e, emin) - m)
+
+
+def within_one_step(got_bits: np.ndarray, r: np.ndarray, dtype: str) -> np.ndarray:
+    """True where the stored value is within one unit in the last place of the
+    cache format (one e4m3 step for E4M3) of the fp32 result ``r`` -- the bar
+    the north star sets: 1 bf16 ulp, or 1 e4m3 step, of the fp32 rotation."""
+    r = np.asarray(r, dtype=np.float64)
+    if dtype == E4M3:
+        r = np.clip(r, -E4M3_MAX, E4M3_MAX)
+    got = to_f32(got_bits, dtype).astype(np.float64)
+    return np.abs(got - r) <= ulp_of(r, dtype)

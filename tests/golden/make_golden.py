@@ -16,6 +16,9 @@ What is recorded (all produced by the reference's own functions on CPU):
                      path, shift_kernels.py:141-159) at the geometry of
                      tests/test_shift_kernels.py:46-78 (8 heads, 128 dim, block 16,
                      a scattered block table, the run starting mid-block)
+* ``f32r_k_<d>``     the same call on fp32 copies of those rows and an fp32 cache:
+                     the reference's rotation computed in fp32, before any rounding
+                     to the cache dtype (the value the 1-ulp bar is measured from)
 * ``f32_digest_*``   sha256 of the fp32 rows ``scatter_shifted`` lands at the Qwen3
                      geometry of tests/test_shift_kernels.py:93-134, both layouts
 * ``slots_*``        ``shift_store.slots`` incl. the known answer [30, 31, 12, 13]
@@ -105,6 +108,13 @@ def main() -> None:
                 assert np.array_equal(bits[..., d:], out["bf16_src"][..., d:])
             else:
                 assert np.array_equal(bits[..., :d], out[f"bf16_k_{delta}"]), "layout changed values"
+            if not hnd:
+                # the unrounded value r: the same torch path on fp32 copies of
+                # the inputs, so the rotation's result is never cast to bf16
+                kv32 = torch.zeros(shape, dtype=torch.float32)
+                sk.scatter_shifted_torch(src.float(), kv32, slots, bs, hnd,
+                                         sk.rope_shift(delta, d, inv, "cpu"))
+                out[f"f32r_k_{delta}"] = kv32[blk, off][..., :d].numpy().copy()
             # everything not in `slots` must still be zero
             mask = torch.ones(nblocks * bs, dtype=torch.bool)
             mask[slots] = False
