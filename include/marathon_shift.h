@@ -107,9 +107,12 @@ MSHIFT_API int mshift_rope_tables(const int64_t* deltas, int32_t n, const float*
 
 /*
  * One layer, one run: write src rows [n, heads, 2*head_size] into the paged
- * cache at slots[n], K rotated by `table` (NULL = plain scatter).  For E4M3,
- * k_scale points at the layer's K scale on the device (dequantise -> rotate
- * -> requantise); V is always copied bit for bit.
+ * cache at slots[n], K rotated by `table` (NULL = plain scatter).  V is always
+ * copied bit for bit.  E4M3 (dequantise -> rotate -> requantise with the
+ * layer's K scale): the scale cancels, so the codes' values are rotated in
+ * fp32 and rounded once to e4m3 (saturating, nearest even) -- within one
+ * e4m3 step of the step-by-step result.  k_scale (device, the layer's K
+ * scale) is therefore not read and may be NULL.
  * Replaces: the Triton launch _shift_scatter_kernel[grid](...) of
  * scatter_shifted (src/marathon/shift_kernels.py:89-132, :166-210).
  */
@@ -124,7 +127,9 @@ MSHIFT_API int mshift_scatter_shifted(const void* src, int64_t src_tok_stride,
  * Batched load: every run x every layer in one persistent launch.  For layer
  * l and run r, store_ptrs[r.session * n_layers + l] rows
  * [r.store_start, +r.len) are written to the paged cache of layer l
- * (k_ptrs[l], v_ptrs[l]) with K rotated by tables[r.table].
+ * (k_ptrs[l], v_ptrs[l]) with K rotated by tables[r.table].  E4M3 caches are
+ * rotated as in mshift_scatter_shifted; k_scales (per-layer K scales) is not
+ * read and may be NULL.
  * tiles_per_layer = sum over runs of ceil(len / tile_tokens); each run's
  * tile_begin is the exclusive prefix of that sum (mshift_plan_tiles fills it).
  * With n_tables > 0 the kernel is launched with programmatic stream

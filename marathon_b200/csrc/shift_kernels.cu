@@ -28,7 +28,10 @@
 // separately, then one fp32 add; no FMA contraction (__fmul_rn/__fadd_rn), so
 // the fp32 value before the final rounding is bit-identical to the CPU
 // computation and the stored element is its round-to-nearest-even.  E4M3:
-// code -> fp32 * k_scale, rotate, / k_scale, saturate to +-448, RNE.
+// the layer's K scale cancels between dequantisation and requantisation, so
+// the codes' values are rotated (fp32, fused multiply-add) and rounded once to
+// e4m3 (saturating at +-448, RNE): within one e4m3 step of the step-by-step
+// dequantise -> rotate -> divide result.
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -152,97 +155,54 @@ struct E4m3 {
   }
 };
 
-// e4m3 requantisation: the code of r / s must be exactly the saturating
-// round-to-nearest-even of the correctly rounded quotient __fdiv_rn(r, s).
-// With inv = 1/s rounded, idn = inv*(1-2^-21) and iup = inv*(1+2^-21) (both
-// rounded), r*idn and r*iup lie more than 4 ulp below and above the quotient
-// (three roundings of 2^-24 against a 2^-21 offset).  Converting both ends
-// gives the same code exactly when every value in between -- the rounded
-// quotient included -- rounds to that code (the conversion is monotonic).
-// Where the two ends differ (a value next to an e4m3 rounding boundary), the
-// quotient is formed by division.
+// e4m3: dequantise with the layer's K scale s, rotate, requantise with the
+// same s.  The scale cancels: (code*s*c - code'*s*sn) / s = code*c - code'*sn,
+// so the kernel rotates the codes' values directly and rounds once to e4m3
+// (saturating at +-448, nearest even).  In fp32 the result differs from the
+// dequantise -> rotate -> divide sequence by a few fp32 ulps of the terms
+// (|terms| <= 448), far below half the smallest e4m3 step (2^-10), so the two
+// codes agree except next to an e4m3 rounding boundary, where they are one
+// step apart: the north star's tolerance for FP8 (1 e4m3 step).
 __device__ __forceinline__ uint32_t cvt_e4m3x2(float2 v) {
   return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3));
 }
 
-// Codes of the four values r[0..1] (one 32-bit word) from the low end; ORs
-// the low-end / high-end difference into `miss`.
-__device__ __forceinline__ uint32_t requant4(const float2* r, float2 idn, float2 iup,
-                                             uint32_t& miss) {
-  const uint32_t lo = cvt_e4m3x2(__fmul2_rn(r[0], idn)) | (cvt_e4m3x2(__fmul2_rn(r[1], idn)) << 16);
-  const uint32_t hi = cvt_e4m3x2(__fmul2_rn(r[0], iup)) | (cvt_e4m3x2(__fmul2_rn(r[1], iup)) << 16);
-  miss |= lo ^ hi;
-  return lo;
-}
-
-__device__ __forceinline__ uint32_t requant4_div(const float2* r, float s) {
-  const float2 e0 = make_float2(__fdiv_rn(r[0].x, s), __fdiv_rn(r[0].y, s));
-  const float2 e1 = make_float2(__fdiv_rn(r[1].x, s), __fdiv_rn(r[1].y, s));
-  return cvt_e4m3x2(e0) | (cvt_e4m3x2(e1) << 16);
-}
-
-// Dequantise and rotate one word pair of e4m3 codes: ra = x*c - y*s and
-// rb = y*c + x*s with x, y = code * scale, every product rounded on its own
-// (packed multiplies; the sums are scalar so no multiply is fused into them).
-__device__ __forceinline__ void rotate_word_e4m3(uint32_t aw, uint32_t bw, const float* cs,
-                                                 const float* sn, float scale, float2* ra,
-                                                 float2* rb) {
+// Rotate one 32-bit word pair of e4m3 codes (elements 4w..4w+3 of each half):
+// ra = x*c - y*sn and rb = y*c + x*sn, as packed fp32x2 products and fused
+// multiply-adds.
+__device__ __forceinline__ void rotate_word_e4m3(uint32_t& aw, uint32_t& bw, const float* cs,
+                                                 const float* sn) {
   float x[4], y[4];
   E4m3::unpack(aw, x);
   E4m3::unpack(bw, y);
   const float4 c4 = *reinterpret_cast<const float4*>(cs);
   const float4 s4 = *reinterpret_cast<const float4*>(sn);
-  const float2 sc = make_float2(scale, scale);
   const float2 c01 = make_float2(c4.x, c4.y), c23 = make_float2(c4.z, c4.w);
   const float2 s01 = make_float2(s4.x, s4.y), s23 = make_float2(s4.z, s4.w);
-  const float2 x01 = __fmul2_rn(make_float2(x[0], x[1]), sc);
-  const float2 x23 = __fmul2_rn(make_float2(x[2], x[3]), sc);
-  const float2 y01 = __fmul2_rn(make_float2(y[0], y[1]), sc);
-  const float2 y23 = __fmul2_rn(make_float2(y[2], y[3]), sc);
-  {
-    const float2 xc = __fmul2_rn(x01, c01), ys = __fmul2_rn(y01, s01);
-    const float2 yc = __fmul2_rn(y01, c01), xs = __fmul2_rn(x01, s01);
-    ra[0] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
-    rb[0] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-  }
-  {
-    const float2 xc = __fmul2_rn(x23, c23), ys = __fmul2_rn(y23, s23);
-    const float2 yc = __fmul2_rn(y23, c23), xs = __fmul2_rn(x23, s23);
-    ra[1] = make_float2(__fsub_rn(xc.x, ys.x), __fsub_rn(xc.y, ys.y));
-    rb[1] = make_float2(__fadd_rn(yc.x, xs.x), __fadd_rn(yc.y, xs.y));
-  }
+  const float2 x01 = make_float2(x[0], x[1]), x23 = make_float2(x[2], x[3]);
+  const float2 y01 = make_float2(y[0], y[1]), y23 = make_float2(y[2], y[3]);
+  const float2 ys01 = __fmul2_rn(y01, s01), ys23 = __fmul2_rn(y23, s23);
+  const float2 xs01 = __fmul2_rn(x01, s01), xs23 = __fmul2_rn(x23, s23);
+  const float2 ra01 = __ffma2_rn(x01, c01, make_float2(-ys01.x, -ys01.y));
+  const float2 ra23 = __ffma2_rn(x23, c23, make_float2(-ys23.x, -ys23.y));
+  const float2 rb01 = __ffma2_rn(y01, c01, xs01);
+  const float2 rb23 = __ffma2_rn(y23, c23, xs23);
+  aw = cvt_e4m3x2(ra01) | (cvt_e4m3x2(ra23) << 16);
+  bw = cvt_e4m3x2(rb01) | (cvt_e4m3x2(rb23) << 16);
 }
 
 // Rotate one pair of partner vectors in place: `a` holds elements
 // [i0, i0+VEC) of the first rotary half, `b` the same elements of the second.
-// Works one 32-bit word (kPer elements) at a time to keep few values live; the
-// products of two elements share one packed fp32x2 multiply (each lane rounds
-// on its own), the sums are scalar, so the results are those of the scalar
-// __fmul_rn / __fsub_rn / __fadd_rn sequence.  For e4m3, each word is
-// requantised from the two interval ends; a word whose ends disagree is
-// requantised by division instead.
+// Works one 32-bit word (kPer elements) at a time to keep few values live.
+// 16/32-bit types: the products of two elements share one packed fp32x2
+// multiply (each lane rounds on its own), the sums are scalar, so the results
+// are those of the scalar __fmul_rn / __fsub_rn / __fadd_rn sequence -- the
+// reference's operation order, rounded once to the cache type.
 template <class E>
-__device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, const float* sn,
-                                            float scale, float inv_scale) {
+__device__ __forceinline__ void rotate_pair(Vec& a, Vec& b, const float* cs, const float* sn) {
   if constexpr (E::kScaled) {
-    const float dn = __fmul_rn(inv_scale, 0.99999952316284180f);  // inv * (1 - 2^-21)
-    const float up = __fmul_rn(inv_scale, 1.00000047683715820f);  // inv * (1 + 2^-21)
-    const float2 idn = make_float2(dn, dn), iup = make_float2(up, up);
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      float2 ra[2], rb[2];
-      rotate_word_e4m3(a.w[w], b.w[w], cs + 4 * w, sn + 4 * w, scale, ra, rb);
-      uint32_t m = 0;
-      const uint32_t la = requant4(ra, idn, iup, m);
-      const uint32_t lb = requant4(rb, idn, iup, m);
-      if (m != 0u) {  // rare: an end sits across an e4m3 rounding boundary
-        a.w[w] = requant4_div(ra, scale);
-        b.w[w] = requant4_div(rb, scale);
-      } else {
-        a.w[w] = la;
-        b.w[w] = lb;
-      }
-    }
+    for (int w = 0; w < 4; ++w) rotate_word_e4m3(a.w[w], b.w[w], cs + 4 * w, sn + 4 * w);
   } else {
     constexpr int P = E::kPer;
 #pragma unroll
@@ -296,7 +256,6 @@ struct KArgs {
   int32_t heads;
   int32_t n_tables;
   const float* tables;       // [n_tables][2][half]
-  const float* k_scales;     // [n_layers] (E4M3 only)
   uint32_t* err;
   // diagnostic hook of the TMA load kernel: 0 = normal; n > 0 bounds every
   // consumer warp's first full-barrier wait to n - 1 rounds
@@ -403,8 +362,6 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
     const int t0 = (tile - run.tile_begin) * a.tile_tokens;
     const int nt = min(a.tile_tokens, run.len - t0);
     const bool tile_ok = ok_desc && nt > 0 && t0 >= 0;
-    const float kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
-    const float kinv = E::kScaled ? __frcp_rn(kscale) : 1.0f;
 
     __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn
     if (threadIdx.x == 0 && bits) atomicOr(a.err, bits);
@@ -495,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
       for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
         if (rotate)
-          rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC, kscale, kinv);
+          rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC);
         if (SAVE) {
           store_vec(sp[q] + ka * 16, k[q][0]);
           store_vec(sp[q] + kb * 16, k[q][1]);
@@ -641,8 +598,6 @@ __device__ __forceinline__ Vec lds_vec(const unsigned char* p) {
 struct BulkMeta {
   char* kbase;
   char* vbase;
-  float kscale;
-  float kinv;  // 1 / kscale rounded (e4m3 requantisation)
   int nt;      // tokens staged (0: nothing to do for this stage)
   int rotate;  // the stage's table row is valid
 };
@@ -711,7 +666,6 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
     const float* tab = nullptr;
     uint32_t desc_bits = 0;
     bool desc_ok = false;
-    float kscale = 1.0f;
     int k = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
       const int s = k % NS;
@@ -760,7 +714,6 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
         tab = nullptr;
         if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
         else if (run.table != -1) { desc_ok = false; desc_bits |= MSHIFT_EBIT_TABLE; }
-        kscale = (E::kScaled && a.k_scales != nullptr) ? a.k_scales[layer] : 1.0f;
       }
       uint32_t bits = desc_bits;
       const bool ok = desc_ok;
@@ -803,8 +756,6 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
         BulkMeta m;
         m.kbase = kbase;
         m.vbase = vbase;
-        m.kscale = kscale;
-        m.kinv = E::kScaled ? __frcp_rn(kscale) : 1.0f;
         m.nt = nvalid > 0 ? nt : 0;
         m.rotate = (HALF > 0 && tab != nullptr) ? 1 : 0;
         s_meta[s] = m;
@@ -898,7 +849,7 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
 #pragma unroll
       for (int q = 0; q < U; ++q) {
         if (!live[q]) continue;
-        if (rotate) rotate_pair<E>(kv[q][0], kv[q][1], tc, ts, m.kscale, m.kinv);
+        if (rotate) rotate_pair<E>(kv[q][0], kv[q][1], tc, ts);
         store_vec(kp[q] + ka * 16, kv[q][0]);
         store_vec(kp[q] + kb * 16, kv[q][1]);
         store_vec(vp[q] + g * 16, vv[q][0]);
@@ -1146,10 +1097,8 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
     return MSHIFT_EINVAL;
   const Variant* v = find_variant(paged->dtype, paged->head_size, rotary, save);
   if (v == nullptr) return MSHIFT_EUNSUPPORTED;
-  if (!save && n_tables > 0) {
-    if (tables == nullptr) return MSHIFT_EINVAL;
-    if (paged->dtype == MSHIFT_E4M3 && k_scales == nullptr) return MSHIFT_EINVAL;
-  }
+  (void)k_scales;  // e4m3: the layer's K scale cancels (see rotate_word_e4m3)
+  if (!save && n_tables > 0 && tables == nullptr) return MSHIFT_EINVAL;
   KArgs a{};
   a.runs = runs;
   a.n_runs = n_runs;
@@ -1171,7 +1120,6 @@ int batched(bool save, const mshift_paged* paged, int32_t rotary, const mshift_r
   a.heads = paged->heads;
   a.n_tables = save ? 0 : n_tables;
   a.tables = save ? nullptr : tables;
-  a.k_scales = save ? nullptr : k_scales;
   a.err = err;
   a.first_wait = g_first_wait.load(std::memory_order_relaxed);
   const int64_t row_elems = (int64_t)paged->heads * 2 * paged->head_size;
@@ -1233,7 +1181,7 @@ int mshift_scatter_shifted(const void* src, int64_t src_tok_stride, int64_t src_
     return MSHIFT_EINVAL;
   const Variant* v = find_variant(paged->dtype, paged->head_size, rotary, false);
   if (v == nullptr) return MSHIFT_EUNSUPPORTED;
-  if (table != nullptr && paged->dtype == MSHIFT_E4M3 && k_scale == nullptr) return MSHIFT_EINVAL;
+  (void)k_scale;  // e4m3: the layer's K scale cancels (see rotate_word_e4m3)
   const int32_t tt = mshift_default_tile_tokens(paged->heads);
   KArgs a{};
   a.runs = nullptr;
@@ -1250,7 +1198,6 @@ int mshift_scatter_shifted(const void* src, int64_t src_tok_stride, int64_t src_
   a.head_stride = paged->head_stride;
   a.num_slots = paged->num_blocks * paged->block_size;
   a.heads = paged->heads;
-  a.k_scales = k_scale;
   a.err = err;
   a.run0 = mshift_run{};
   a.run0.store_start = 0;
@@ -1437,7 +1384,7 @@ int check_load_args(const mshift_paged* paged, int32_t rotary, const mshift_run*
                     int32_t n_runs, int32_t tile_tokens, int32_t tiles_per_layer,
                     int32_t n_layers, void* const* store_ptrs, const int64_t* store_caps,
                     int32_t n_sessions, int64_t st_tok, int64_t st_head, void* const* k_ptrs,
-                    void* const* v_ptrs, const float* k_scales, bool rotating, uint32_t* err) {
+                    void* const* v_ptrs, uint32_t* err) {
   int st = check_paged(paged);
   if (st != MSHIFT_OK) return st;
   if (runs == nullptr || n_runs <= 0 || n_layers <= 0 || tiles_per_layer <= 0) return MSHIFT_EINVAL;
@@ -1452,7 +1399,6 @@ int check_load_args(const mshift_paged* paged, int32_t rotary, const mshift_run*
     return MSHIFT_EINVAL;
   if (find_variant(paged->dtype, paged->head_size, rotary, false) == nullptr)
     return MSHIFT_EUNSUPPORTED;
-  if (rotating && paged->dtype == MSHIFT_E4M3 && k_scales == nullptr) return MSHIFT_EINVAL;
   return MSHIFT_OK;
 }
 
@@ -1473,7 +1419,7 @@ int mshift_load_noalloc(const mshift_paged* paged, int32_t rotary, const mshift_
   if (n_deltas > 0 && (deltas == nullptr || inv_freq == nullptr)) return MSHIFT_EINVAL;
   int st = check_load_args(paged, rotary, runs, n_runs, tile_tokens, tiles_per_layer, n_layers,
                            store_ptrs, store_caps, n_sessions, st_tok, st_head, k_ptrs, v_ptrs,
-                           k_scales, n_deltas > 0, err);
+                           err);
   if (st != MSHIFT_OK) return st;
   float* tables = nullptr;
   st = noalloc_tables(&tables);

@@ -202,8 +202,10 @@ def scatter_shifted(
     ``slot % block_size``), ``hnd`` selects the fused layout, ``shift=None`` or
     delta 0 is a plain scatter, ``n == 0`` is a no-op.  ``src`` must have the
     cache's dtype (the store holds cache-dtype rows).  E4M3 caches
-    (``float8_e4m3fn``, or ``uint8`` with ``fp8=True``) need ``k_scale``, a
-    one-element fp32 device tensor.  ``check=True`` synchronises and raises on
+    (``float8_e4m3fn``, or ``uint8`` with ``fp8=True``) are dequantised,
+    rotated and requantised with the layer's K scale, which cancels: the
+    kernel rotates the codes' values and rounds once, so ``k_scale`` is
+    accepted for the reference's call shape but not needed.  ``check=True`` synchronises and raises on
     any token the kernel rejected; otherwise rejections accumulate for
     :func:`take_errors`.
     """
@@ -228,12 +230,7 @@ def scatter_shifted(
     rotate = shift is not None and shift.delta != 0
     rotary = shift.rotary if shift is not None else geo.head_size
     table_ptr = shift.table.data_ptr() if rotate else None
-    ks_ptr = None
-    if geo.dtype == _lib.E4M3 and rotate:
-        if k_scale is None:
-            raise ShiftError("an e4m3 cache needs k_scale to re-rotate keys")
-        k_scale = k_scale.to(device=kv.device, dtype=torch.float32).reshape(-1)[:1].contiguous()
-        ks_ptr = k_scale.data_ptr()
+    ks_ptr = None  # e4m3: the K scale cancels; the kernel does not read it
     err = _err_word(kv.device)
     k_base = kv.data_ptr()
     v_base = k_base + geo.head_size * geo.elem_bytes
@@ -721,16 +718,12 @@ class Launcher:
         _require_cuda(inv_freq, "inv_freq")
         n_layers = self.layer_range(first_layer, n_layers)
         deltas = sorted({int(r.delta) for r in runs if int(r.delta) != 0})
-        if self.geo.dtype == _lib.E4M3 and deltas:
-            if k_scales is None:
-                raise ShiftError("an e4m3 cache needs per-layer k_scales to re-rotate keys")
-            k_scales = k_scales.to(device=self.device, dtype=torch.float32).contiguous()
-            if k_scales.numel() < len(self.layers):
-                raise ShiftError("need one K scale per layer")
         p = self._prepare("load", runs, store, deltas, first_layer, n_layers,
                           torch.cuda.current_stream(self.device), upload_stream)
         p.inv_freq = inv_freq if inv_freq.dtype == torch.float32 else inv_freq.float()
-        p.k_scales = k_scales if deltas else None
+        # e4m3: the per-layer K scale cancels between dequantisation and
+        # requantisation, so the kernels never read k_scales
+        p.k_scales = None
         if deltas:
             # per staging slot, so a batch still in flight keeps its tables
             need = len(deltas) * 2 * p.inv_freq.numel()
@@ -821,8 +814,9 @@ class Launcher:
              k_scales: torch.Tensor | None = None, check: bool = True) -> None:
         """Every run x every layer: store rows -> paged cache, K rotated by its delta.
 
-        ``inv_freq`` is the fp32 device tensor of the RoPE inverse frequencies,
-        ``k_scales`` the per-layer fp32 K scales of an e4m3 cache.
+        ``inv_freq`` is the fp32 device tensor of the RoPE inverse frequencies.
+        ``k_scales`` (the per-layer K scales of an e4m3 cache) is accepted and
+        not needed: the scale cancels.
         """
         if not runs:
             return

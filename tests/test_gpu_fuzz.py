@@ -18,6 +18,7 @@ from marathon_b200 import shift_kernels as sk
 from marathon_b200.paged import KVLayers, describe
 from marathon_b200.shift_kernels import Launcher, RunSpec, StoreView
 from oracle import shift_oracle as O
+from parity import assert_cache_matches
 
 pytestmark = pytest.mark.gpu
 
@@ -119,7 +120,10 @@ def test_random_batches_match_the_oracle(cuda, seed, kernel):
     O.load([[_bits(t) for t in per] for per in stores], runs_o, paged, tables, dtype,
            k_scales.numpy())
     for li in range(layers):
-        assert _bits(kv_d[li]).reshape(-1).tobytes() == paged[li].flat.tobytes(), (seed, li)
+        assert_cache_matches(_bits(kv_d[li]), paged[li], dtype, (seed, li))
+        # the save below starts from what the load actually wrote (for e4m3 a
+        # K code may sit one step from the oracle's)
+        paged[li].flat = _bits(kv_d[li]).reshape(-1).copy()
 
     # and the save gathers the landed rows back out
     fresh = [[torch.zeros_like(t) for t in per] for per in st_d]
