@@ -101,9 +101,9 @@ def test_argument_errors_return_before_any_launch(lib):
     odd = _lib.Paged(4096, 2048, 256, 10, 16, 8, 96, _lib.BF16)
     assert lib.mshift_load(odd, 96, 16, 1, 32, 1, 1, 8, 8, 1, 2048, 256, 8, 8, None, 0, None,
                            8, None) == _lib.EUNSUPPORTED
-    # e4m3 rotation without scales
+    # rotation tables announced (n_tables = 1) but not passed
     f8 = _lib.Paged(4096, 2048, 256, 10, 16, 8, 128, _lib.E4M3)
-    assert lib.mshift_load(f8, 128, 16, 1, 32, 1, 1, 8, 8, 1, 2048, 256, 8, 8, 8, 1, None,
+    assert lib.mshift_load(f8, 128, 16, 1, 32, 1, 1, 8, 8, 1, 2048, 256, 8, 8, None, 1, None,
                            8, None) == _lib.EINVAL
     # zero-length single scatter is a successful no-op
     assert lib.mshift_scatter_shifted(None, 0, 0, 0, None, None, p, None, None, 128, None, None,
