@@ -96,9 +96,10 @@ typedef struct mshift_run {
 } mshift_run;                   /* 56 bytes, 8-byte aligned                         */
 
 /*
- * Rotation tables for n deltas: tables[d][0][i] = cos(a), tables[d][1][i] =
- * sin(a) with a = fp32(deltas[d]) * inv_freq[i] rounded to fp32, and cos/sin
- * rounded to nearest fp32.  One launch for all deltas.
+ * Rotation tables for n deltas: tables[d][0][i] = cosf(a), tables[d][1][i] =
+ * sinf(a) with a = fp32(deltas[d]) * inv_freq[i] rounded to fp32 -- the
+ * values torch's fp32 cos / sin give on a CUDA device, i.e. the reference's
+ * own tables as its GPU path builds them.  One launch for all deltas.
  * Replaces: marathon rope_shift (src/marathon/shift_kernels.py:68-84), whose
  * cos/sgn/partner tables are this table plus a sign flip and a permutation.
  */

@@ -862,9 +862,12 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
   cta_barrier_1(kBulkThreads);  // the producer drains after every consumer is out
 }
 
-// cos/sin of fp32(delta) * inv_freq[i]: the angle is rounded to fp32 exactly
-// as the reference forms it (src/marathon/shift_kernels.py:73), then cos and
-// sin are evaluated in double precision and rounded once to fp32.
+// cos/sin of fp32(delta) * inv_freq[i], built exactly as the reference
+// builds them on the GPU it serves from (src/marathon/shift_kernels.py:73-79:
+// ``float(delta) * inv_freq`` in fp32, then torch's fp32 ``cos`` / ``sin`` on
+// the cache's CUDA device, which are the CUDA math library's cosf / sinf):
+// the angle is one fp32 product, then cosf and sinf.  With the reference's
+// own tables the rotation that follows is the reference's, bit for bit.
 __global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float* inv_freq,
                                    int32_t half, float* out) {
   allow_dependents();  // the load kernel may launch; it waits for our writes
@@ -873,10 +876,8 @@ __global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float
   const int64_t d = i / half;
   const int64_t j = i - d * half;
   const float ang = __fmul_rn(static_cast<float>(deltas[d]), inv_freq[j]);
-  double s, c;
-  sincos(static_cast<double>(ang), &s, &c);
-  out[d * 2 * half + j] = __double2float_rn(c);
-  out[d * 2 * half + half + j] = __double2float_rn(s);
+  out[d * 2 * half + j] = cosf(ang);
+  out[d * 2 * half + half + j] = sinf(ang);
 }
 
 // ------------------------------------------------------------------ dispatch

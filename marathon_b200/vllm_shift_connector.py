@@ -725,11 +725,12 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         pass/fail bar instead of a logged difference: V and any non-rotary
         tail bit for bit, and every rotated K element within one unit in the
         last place (of the cache dtype) of ``k*cos + rotate_half(k)*sin``
-        evaluated in fp32 with torch's fp32 cos/sin of ``fp32(delta) *
-        inv_freq`` -- the reference's own tables (``shift_kernels.py:68-84``).
-        It runs on the host, on copies of the store rows and of the paged
-        rows, so it shares nothing with the kernel.  Returns False (and logs
-        an error) on any mismatch.
+        evaluated by torch in fp32 with the reference's own tables -- torch's
+        fp32 cos/sin of ``fp32(delta) * inv_freq`` on the cache's device, as
+        its ``rope_shift`` builds them (``shift_kernels.py:68-84``).  Plain
+        torch operations on copies of the store rows and the paged rows: it
+        shares nothing with the kernel.  Returns False (and logs an error) on
+        any mismatch.
         """
         geo = self._worker.layers.geometry
         cache_dtype = self._worker.layers.tensors[0].dtype
@@ -738,18 +739,17 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             return True
         d, rot = geo.head_size, self._rotary
         h = rot // 2
-        ang = float(job.delta) * self._inv_freq.to(torch.float32)
-        cos, sin = torch.cat((ang, ang)).cos(), torch.cat((ang, ang)).sin()
         sl = job.host_slots(self._bs)
-        blk, off = sl // self._bs, sl % self._bs
         bits = {2: torch.int16, 4: torch.int32}[geo.elem_bytes]
         ok = True
         for name, kv in zip(self._worker.layers.names, self._worker.layers.tensors, strict=True):
             row = self._store.read(job.session, name, job.row, job.length)
             if row is None:
                 continue
-            row = row.cpu()
-            b, o = blk.to(kv.device), off.to(kv.device)
+            row = row.to(kv.device)  # a host or peer store tier
+            ang = float(job.delta) * self._inv_freq.to(kv.device, torch.float32)
+            cos, sin = torch.cat((ang, ang)).cos(), torch.cat((ang, ang)).sin()
+            b, o = (sl // self._bs).to(kv.device), (sl % self._bs).to(kv.device)
             if geo.kind == "hnd":
                 got = kv[b, :, o]
             elif geo.kind == "nhd":
@@ -757,7 +757,6 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             else:
                 kk, vv = (kv[0], kv[1]) if geo.kind == "split" else (kv[:, 0], kv[:, 1])
                 got = torch.cat((kk[b, o], vv[b, o]), -1)
-            got = got.cpu()
             kf = row[..., :rot].float()
             want = kf * cos + torch.cat((-kf[..., h:], kf[..., :h]), -1) * sin
             k_off = (got[..., :rot].float() - want).abs() > ulp(want, cache_dtype)

@@ -46,3 +46,20 @@ def assert_k_codes_match(got_k: np.ndarray, want_k: np.ndarray, dtype: str, tag=
     steps = O.ulp_distance(got_k, want_k, O.E4M3)
     assert steps.max() <= 1, (tag, int(steps.max()))
     assert (steps > 0).mean() < 1e-3, (tag, float((steps > 0).mean()))
+
+
+def reference_tables(deltas, inv_freq, device) -> np.ndarray:
+    """``[n, 2, half]`` cos/sin tables exactly as the reference's GPU path builds them
+    (``src/marathon/shift_kernels.py:73-79``): the fp32 angle ``float(delta) *
+    inv_freq`` and torch's fp32 ``cos`` / ``sin`` on the CUDA device.  The oracle
+    rotates with these in the GPU tests, so a bit-exact match covers the tables
+    and the rotation together."""
+    import torch
+
+    inv = torch.as_tensor(np.asarray(inv_freq, dtype=np.float32)).to(device)
+    out = []
+    for d in deltas:
+        ang = float(d) * inv
+        out.append(torch.stack((ang.cos(), ang.sin())).cpu().numpy())
+    return np.stack(out).astype(np.float32) if out else np.zeros((0, 2, inv.numel()),
+                                                                 np.float32)

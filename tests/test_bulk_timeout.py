@@ -26,6 +26,7 @@ def test_a_timed_out_tma_load_flags_writes_nothing_and_the_next_load_is_exact(cu
     from marathon_b200.shift_kernels import (Launcher, RunSpec, ShiftError, StoreView, inv_freq,
                                              set_load_kernel)
     from oracle import shift_oracle as O
+    from parity import reference_tables
 
     lib = _lib.load()
     g = torch.Generator().manual_seed(9)
@@ -63,6 +64,6 @@ def test_a_timed_out_tma_load_flags_writes_nothing_and_the_next_load_is_exact(cu
             pos = np.arange(r.paged_start, r.paged_start + r.length)
             at = got[r.block_table[pos // BS], pos % BS]
             rows = src[r.store_start : r.store_start + r.length]
-            tab = O.rope_tables([r.delta], O.inv_freq(D, 1e6))[0]
+            tab = reference_tables([r.delta], O.inv_freq(D, 1e6), cuda)[0]
             assert np.array_equal(at[..., D:], rows[..., D:])
             assert np.array_equal(at[..., :D], O.shift_k_bits(rows[..., :D], tab, O.BF16))

@@ -17,6 +17,7 @@ vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.ba
 KVConnectorRole = vllm_base.KVConnectorRole
 
 from marathon_b200 import vllm_shift_connector as C  # noqa: E402
+from parity import reference_tables  # noqa: E402
 from vllm_fakes import BS, fake_config, forward_context, new_req, request, sched_output  # noqa: E402,E501
 
 
@@ -217,7 +218,7 @@ def test_worker_save_then_shifted_load_through_the_connector(cuda, shape_kind, b
     from marathon_b200.paged import describe
 
     inv = conn._inv_freq.numpy()
-    tab = O.rope_tables([37], inv)[0]
+    tab = reference_tables([37], inv, cuda)[0]
     sl1 = _oracle_slots(blocks1, 101, 101 + 528)
     sl0 = _oracle_slots(blocks0, 0, 600)
     for name, kv in caches.items():
@@ -292,7 +293,7 @@ def test_extent_mode_three_turns_load_from_generation_zero(cuda, store_device):
         releases=[("s", 1, 0, 50)]), save=False)
 
     inv = conn._inv_freq.numpy()
-    t50, t13 = O.rope_tables([-50, -13], inv)
+    t50, t13 = reference_tables([-50, -13], inv, cuda)
     for name, kv in caches.items():
         got = rows(kv, bt[2], 0, 587)
         want1 = gen1[name][50:137]

@@ -23,6 +23,7 @@ vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.ba
 KVConnectorRole = vllm_base.KVConnectorRole
 
 from marathon_b200 import vllm_shift_connector as C  # noqa: E402
+from parity import reference_tables  # noqa: E402
 from vllm_fakes import BS, fake_config, forward_context, new_req, request, sched_output  # noqa: E402
 
 N_PROMPT = 2000
@@ -173,7 +174,7 @@ def test_gap_filled_request_loads_every_segment_bit_exact(cuda, reference_pkg):
             pos = np.arange(ld.dst_start, ld.dst_start + ld.length)
             filled[pos] = True
             src = rows[name][ld.src_start : ld.src_start + ld.length]
-            tab = O.rope_tables([ld.delta], inv)[0]
+            tab = reference_tables([ld.delta], inv, cuda)[0]
             at = got[bt[pos // BS], pos % BS]
             assert np.array_equal(at[..., D:], src[..., D:]), name
             assert np.array_equal(at[..., :D], O.shift_k_bits(src[..., :D], tab, O.BF16)), name

@@ -18,7 +18,7 @@ from marathon_b200 import shift_kernels as sk
 from marathon_b200.paged import KVLayers, describe
 from marathon_b200.shift_kernels import Launcher, RunSpec, StoreView
 from oracle import shift_oracle as O
-from parity import assert_cache_matches
+from parity import assert_cache_matches, reference_tables
 
 pytestmark = pytest.mark.gpu
 
@@ -109,7 +109,7 @@ def test_random_batches_match_the_oracle(cuda, seed, kernel):
         sk.set_load_kernel(prev)
 
     deltas = sorted({r["delta"] for r in runs_o if r["delta"]})
-    tables = O.rope_tables(deltas, inv.numpy()) if deltas else None
+    tables = reference_tables(deltas, inv.numpy(), cuda) if deltas else None
     for r in runs_o:
         r["table"] = deltas.index(r["delta"]) if r["delta"] else -1
     paged = []

@@ -48,6 +48,7 @@ def _run_batches(cuda, early: bool, monkeypatch):
 @pytest.mark.gpu
 def test_early_upload_with_more_batches_than_slots_behind_a_busy_stream(cuda, monkeypatch):
     from oracle import shift_oracle as O
+    from parity import reference_tables
 
     early, stores, bt = _run_batches(cuda, True, monkeypatch)
     late, _, _ = _run_batches(cuda, False, monkeypatch)
@@ -55,7 +56,7 @@ def test_early_upload_with_more_batches_than_slots_behind_a_busy_stream(cuda, mo
         assert np.array_equal(a, b)
     inv = O.inv_freq(D, 1e6)
     for b in range(BATCHES):
-        tab = O.rope_tables([17 * (b + 1) - 40], inv)[0]
+        tab = reference_tables([17 * (b + 1) - 40], inv, cuda)[0]
         pos = np.arange(64)
         blk = bt[40 * b : 40 * b + 40][pos // BS]
         for layer in range(L):

@@ -19,6 +19,7 @@ from marathon_b200.shift_store import ShiftStore
 from marathon_b200.store_tier import is_staged, plan_chunks
 from marathon_b200.worker import LoadJob, SaveJob, ShiftWorker
 from oracle import shift_oracle as O
+from parity import reference_tables
 
 H, D, BS = 8, 128, 16
 ROW = H * 2 * D * 2  # bytes of one bf16 store row
@@ -173,7 +174,7 @@ def test_host_tier_load_vs_oracle(cuda):
     worker.load(jobs)
     torch.cuda.synchronize()
     deltas = sorted({j.delta for j in jobs if j.delta})
-    tables = O.rope_tables(deltas, sk.inv_freq(D, 1e6).numpy())
+    tables = reference_tables(deltas, sk.inv_freq(D, 1e6).numpy(), cuda)
     runs = []
     for j in jobs:
         r = {"session": int(j.session[1:]), "store_start": j.src_start, "len": j.length,

@@ -15,6 +15,7 @@ import marathon_b200  # noqa: F401  (registers the operators)
 from marathon_b200 import shift_kernels as sk
 from marathon_b200.shift_kernels import ShiftError
 from oracle import shift_oracle as O
+from parity import reference_tables
 
 H, D, BS = 8, 128, 16
 
@@ -61,7 +62,7 @@ def test_shift_load_operator_matches_the_oracle(cuda):
                                   None)
     torch.cuda.synchronize()
     deltas = sorted({s[4] for s in seg if s[4]})
-    tabs = O.rope_tables(deltas, inv.numpy())
+    tabs = reference_tables(deltas, inv.numpy(), cuda)
     runs = [{"session": s, "store_start": a, "len": n, "paged_start": b,
              "block_table": tables[s], "table": deltas.index(d) if d else -1}
             for s, a, b, n, d in seg]
