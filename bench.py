@@ -18,12 +18,17 @@ NCCL traffic is one broadcast of the segment table at set-up.  `value` is the
 whole turn's algorithmic bytes over the max-over-ranks device time.
 
 Printed JSON keys beyond the driver's base contract:
-  roofline      load kernel alone: algorithmic bytes per launch / mean CUDA-event
+  roofline      load kernel: algorithmic bytes per launch / mean CUDA-event
                 duration of that launch, against the measured HBM copy peak
   e2e           the same turn through the public worker API (ShiftWorker.load)
                 from host metadata: block table + descriptors copied from pinned
-                host memory, tables + load kernels, the 4-byte status read back
+                host memory, tables + load kernels, the 4-byte status read back;
+                loads are queued back to back and each status is read when the
+                next load has been queued (the last one inside the timed region)
   cpu_baseline  the reference's torch CPU path on this host, bounded sample
+  c3            (N=1, default config) the FP8 turn: kernel, e2e, roofline and a
+                check against a torch restatement of dequantise/rotate/requantise
+  c4            (N>1, default config) 64 sessions in one launch per rank at TP N
 """
 
 from __future__ import annotations
@@ -65,7 +70,27 @@ def parse():
     ap.add_argument("--no-alt", action="store_true", help="skip the TMA bulk-load timing")
     ap.add_argument("--no-host-tier", action="store_true",
                     help="skip the pinned-host store tier timing (N=1 only)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the c3 (N=1) / c4 (N>1) lines of the default run")
+    ap.add_argument("--no-triton", action="store_true",
+                    help="reference arm: skip the reference's Triton kernel on the GPU")
     return ap.parse_args()
+
+
+def workload_config(cfg, world: int, layout: str) -> dict:
+    """The ``config`` object of both arms' lines: the workload only, identical in both."""
+    from marathon_b200.sharding import head_shard
+
+    lo, hi = head_shard(cfg.heads, 0, world)
+    return {
+        "workload": f"{cfg.name} {cfg.model} shift turn", "layers": cfg.layers,
+        "sessions": cfg.sessions, "tokens_shifted": cfg.shifted_tokens,
+        "deltas": sorted({s.delta for segs in cfg.segments for s in segs}),
+        "heads": cfg.heads, "heads_per_rank": hi - lo, "head_size": cfg.head_size,
+        "block_size": cfg.block_size, "kv_dtype": cfg.dtype, "layout": layout,
+        "parallelism": f"kv-head shard tp{world}", "turn_bytes": cfg.algorithmic_bytes(),
+        "l2": "inputs larger than L2 (store + paged cache per step >> 126 MB)",
+    }
 
 
 # ----------------------------------------------------------------- helpers
@@ -143,8 +168,32 @@ class Clocks:
 
 
 # --------------------------------------------------------- CPU baseline
+def reference_shift_module():
+    """The reference's own ``marathon.shift_kernels``, unmodified, from ``baseline/_ref``
+    (installed by ``baseline/install_ref.py``); None when it is not installed."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "marathon" / "shift_kernels.py").is_file():
+        return None
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    import marathon.shift_kernels as ref_sk
+
+    return ref_sk
+
+
 class CpuPath:
-    """The reference's torch CPU path on two resident layers of ``cfg``'s first segment."""
+    """The reference's torch CPU path over ``cfg``'s first segment, one layer per call.
+
+    bf16: the reference's own ``scatter_shifted_torch`` with tables from its own
+    ``rope_shift(delta, head_size, inv_freq, "cpu")`` (``src/marathon/
+    shift_kernels.py:68-84``, ``:141-159``), imported from ``baseline/_ref``
+    (``kind`` "reference"); without that install, or for e4m3 (the reference
+    has no scale handling), the restatement in ``oracle/torch_cpu_path.py``
+    (``kind`` "port").  ``LAYERS`` distinct layers of store rows and paged
+    cache are cycled, a working set far larger than the host's caches.
+    """
+
+    LAYERS = 4
 
     def __init__(self, cfg):
         from oracle import shift_oracle as O
@@ -155,41 +204,61 @@ class CpuPath:
         self.threads = os.cpu_count() or 1
         torch.set_num_threads(self.threads)
         seg = cfg.segments[0][0]
+        self.seg = seg
         self.n, h, d, bs = seg.length, cfg.heads, cfg.head_size, cfg.block_size
         blocks = -(-seg.dst_end // bs) + 16
         table = np.random.default_rng(0).permutation(blocks).astype(np.int64)
         self.slots = torch.from_numpy(O.slots(table, seg.dst_start, seg.dst_end, bs))
-        inv = O.inv_freq(d, cfg.theta)
-        self.emb = T.emb_tables(torch.from_numpy(O.rope_tables([seg.delta], inv)[0]))
+        self.inv = 1.0 / (cfg.theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
         g = torch.Generator().manual_seed(0)
         self.fp8 = cfg.dtype == "e4m3"
+        self.ref = None if self.fp8 else reference_shift_module()
+        self.kind = "reference" if self.ref is not None else "port"
         if self.fp8:  # codes of the c3 distribution: values / per-layer scale, saturated
             self.k_scale = 0.05
             self.srcs = [(torch.randn(self.n, h, 2 * d, generator=g) * 20).clamp(-448, 448)
-                         .to(torch.float8_e4m3fn) for _ in range(2)]
+                         .to(torch.float8_e4m3fn) for _ in range(self.LAYERS)]
             self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.float8_e4m3fn)
-                        for _ in range(2)]
+                        for _ in range(self.LAYERS)]
         else:
             self.srcs = [torch.randn(self.n, h, 2 * d, generator=g).to(torch.bfloat16)
-                         for _ in range(2)]
-            self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.bfloat16) for _ in range(2)]
+                         for _ in range(self.LAYERS)]
+            self.kvs = [torch.zeros(blocks, bs, h, 2 * d, dtype=torch.bfloat16)
+                        for _ in range(self.LAYERS)]
         self.bs = bs
         self.i = 0
-        self.run(tokens=256)  # first touch
+        self.run(layers=1, tokens=256)  # first touch
 
-    def run(self, tokens: int | None = None) -> tuple[float, int]:
-        """One layer (or its first ``tokens`` tokens); returns (seconds, bytes moved)."""
+    @property
+    def impl(self) -> str:
+        if self.ref is not None:
+            return "marathon.shift_kernels.scatter_shifted_torch (reference, baseline/_ref)"
+        return "oracle/torch_cpu_path.py (restated torch path)"
+
+    def run(self, layers: int = 1, tokens: int | None = None) -> tuple[float, int]:
+        """``layers`` layer scatters of one turn (tables built once, as per load);
+        returns (seconds, algorithmic bytes moved)."""
         n = self.n if tokens is None else min(tokens, self.n)
-        k = self.i % 2
-        self.i += 1
+        d = self.cfg.head_size
         t0 = time.perf_counter()
-        if self.fp8:
-            self.T.scatter_layer_e4m3(self.srcs[k][:n], self.kvs[k], self.slots[:n], self.bs,
-                                      False, self.emb, self.k_scale)
+        if self.ref is not None:
+            shift = self.ref.rope_shift(self.seg.delta, d, self.inv, "cpu")
         else:
-            self.T.scatter_layer(self.srcs[k][:n], self.kvs[k], self.slots[:n], self.bs, False,
-                                 self.emb)
-        return time.perf_counter() - t0, n * self.cfg.bytes_per_token_layer()
+            from oracle import shift_oracle as O
+
+            emb = self.T.emb_tables(torch.from_numpy(
+                O.rope_tables([self.seg.delta], self.inv.numpy())[0]))
+        for _ in range(layers):
+            k = self.i % self.LAYERS
+            self.i += 1
+            src, kv, sl = self.srcs[k][:n], self.kvs[k], self.slots[:n]
+            if self.ref is not None:
+                self.ref.scatter_shifted_torch(src, kv, sl, self.bs, False, shift)
+            elif self.fp8:
+                self.T.scatter_layer_e4m3(src, kv, sl, self.bs, False, emb, self.k_scale)
+            else:
+                self.T.scatter_layer(src, kv, sl, self.bs, False, emb)
+        return time.perf_counter() - t0, layers * n * self.cfg.bytes_per_token_layer()
 
     def sample(self, seconds: float) -> dict:
         done = moved = 0
@@ -203,47 +272,107 @@ class CpuPath:
                 "ms_per_layer": el / done * 1e3,
                 "sample": f"{done} layer(s) of {self.cfg.name}: {self.n} tokens x "
                           f"{self.cfg.heads} heads x {2 * self.cfg.head_size} "
-                          f"{self.cfg.dtype} each, torch CPU, {self.threads} threads"}
+                          f"{self.cfg.dtype} each, {self.impl}, {self.threads} threads"}
+
+
+def reference_triton(cfg, steps: int, warmup: int) -> dict:
+    """The reference's unmodified Triton kernel on this GPU, one launch per layer.
+
+    ``marathon.shift_kernels.scatter_shifted`` (``src/marathon/shift_kernels.py:
+    162-210``) from ``baseline/_ref``: per turn, the tables of the load's delta
+    (``rope_shift`` on the device) and one ``_shift_scatter_kernel`` launch per
+    layer over the store rows, with the destination slots already on the
+    device.  CUDA events around whole turns.
+    """
+    ref_sk = reference_shift_module()
+    if ref_sk is None or not getattr(ref_sk, "HAVE_TRITON", False):
+        return {"unavailable": "the reference package or Triton is not importable"}
+    from marathon_b200.workloads import build
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = build(cfg, dev)
+    r = wl.runs[0]
+    bt = r.block_table.long()
+    pos = torch.arange(r.paged_start, r.paged_start + r.length, device=dev)
+    slots = bt[pos // cfg.block_size] * cfg.block_size + pos % cfg.block_size
+    inv = 1.0 / (cfg.theta ** (torch.arange(0, cfg.head_size, 2, dtype=torch.float32)
+                               / cfg.head_size))
+    srcs = [wl.stores[0][li][r.store_start : r.store_start + r.length] for li in range(cfg.layers)]
+
+    def turn():
+        shift = ref_sk.rope_shift(r.delta, cfg.head_size, inv, dev)
+        for src, kv in zip(srcs, wl.kv, strict=True):
+            ref_sk.scatter_shifted(src, kv, slots, cfg.block_size, False, shift)
+
+    ref_sk.warmup(wl.kv[0], cfg.block_size, False)
+    for _ in range(max(warmup, 1)):
+        turn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        turn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    out = {"impl": "marathon.shift_kernels.scatter_shifted -> _shift_scatter_kernel "
+                   "(reference Triton kernel, unmodified, baseline/_ref)",
+           "value": round(cfg.algorithmic_bytes() / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "ms_per_turn": round(ms, 4), "launches_per_turn": cfg.layers,
+           "device": torch.cuda.get_device_name(dev), "steps": steps,
+           "note": "destination slots resident on the device; CUDA events around whole turns"}
+    del wl, srcs
+    torch.cuda.empty_cache()
+    return out
 
 
 def reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from marathon_b200.workloads import config
 
     cfg = config(args.config)
-    seg = cfg.segments[0][0]
     cpu = CpuPath(cfg)
     t_layer, _ = cpu.run()
-    # each step is a bounded slice of one layer so K + W steps fit in about two minutes
-    budget = 120.0 / max(args.steps + args.warmup, 1)
-    tokens = max(256, min(seg.length, int(seg.length * budget / max(t_layer, 1e-6))))
-    secs = moved = 0.0
+    # a step is one whole turn (every layer) unless K + W whole turns would take
+    # more than about 150 s, in which case each step is a bounded run of layers
+    budget = 150.0
+    per_step = cfg.layers
+    if (args.steps + args.warmup) * t_layer * cfg.layers > budget:
+        per_step = max(1, int(budget / max((args.steps + args.warmup) * t_layer, 1e-9)))
+    times, moved = [], 0
     for i in range(args.warmup + args.steps):
-        dt, b = cpu.run(tokens)
+        dt, b = cpu.run(layers=per_step)
         if i >= args.warmup:
-            secs += dt
+            times.append(dt)
             moved += b
+    secs = sum(times)
     gbs = moved / secs / 1e9
-    ms_turn = cfg.algorithmic_bytes() / (gbs * 1e9) * 1e3
+    ms_step = secs / args.steps * 1e3
+    whole = per_step == cfg.layers
+    sample = (f"each step: one whole {cfg.name} turn ({cfg.layers} layers x {cpu.n} tokens)"
+              if whole else f"each step: {per_step} of {cfg.layers} layers x {cpu.n} tokens")
     line = {
-        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_turn, 3),
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": cfg.dtype, "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"{cfg.name} {cfg.model} shift turn", "layers": cfg.layers,
-                   "tokens_shifted": seg.length, "delta": seg.delta, "heads": cfg.heads,
-                   "head_size": cfg.head_size, "block_size": cfg.block_size, "layout": "nhd",
-                   "turn_bytes": cfg.algorithmic_bytes()},
+        "dtype": "e4m3" if cfg.dtype == "e4m3" else "bf16", "data": "synthetic",
+        "impl": "reference", "config": workload_config(cfg, world, args.layout),
+        "ms_per_turn": round(ms_step * cfg.layers / per_step, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads,
-                         "kind": "port",
-                         "sample": f"each step: {tokens} of {seg.length} tokens of one layer "
-                                   "(torch CPU path); ms_per_step extrapolates to the "
-                                   f"{cfg.layers}-layer turn"},
+                         "kind": cpu.kind, "impl": cpu.impl,
+                         "sample": sample + f", torch CPU, {cpu.threads} threads"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if world == 1 and not args.no_triton and cpu.ref is not None and torch.cuda.is_available():
+        try:
+            line["reference_gpu"] = reference_triton(cfg, max(args.steps, 5), args.warmup)
+        except Exception as e:  # noqa: BLE001 - report, never fail the CPU arm over it
+            line["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     print(json.dumps(line), flush=True)
 
 
@@ -339,25 +468,272 @@ def host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device) -> dic
     }
 
 
-def native_arm(args) -> None:
-    import torch.distributed as dist
+class Ranks:
+    """This process's rank, the device and the group's barrier / max over ranks."""
 
-    from marathon_b200.paged import KVLayers
-    from marathon_b200.sharding import broadcast_table, head_shard, pack_table
-    from marathon_b200.shift_kernels import Launcher
+    def __init__(self):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = torch.device("cuda", self.local)
+        torch.cuda.set_device(self.device)
+        if self.world > 1:
+            dist.init_process_group("nccl", device_id=self.device,
+                                    timeout=timedelta(seconds=180))
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier(device_ids=[self.local])
+
+    def max(self, x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.barrier()
+            self.dist.destroy_process_group()
+
+
+def load_step(launcher, wl, ev=None, check=False) -> tuple[int, int]:
+    """One turn: pack + descriptor copy, table and load kernels; (launches, H2D bytes).
+
+    The event pair brackets the table kernel and the load kernel together: an
+    event between them would break the programmatic dependent launch that lets
+    the load kernel's CTAs start while the table kernel ends.
+    """
+    p = launcher.prepare_load(wl.runs, wl.view, wl.inv_freq)
+    if ev is not None:
+        ev[0].record()
+    n = launcher.launch(p)
+    if ev is not None:
+        ev[1].record()
+    launcher.finish(p, check)
+    return n, p.h2d_bytes
+
+
+def timed_turns(step, steps: int, ranks: Ranks) -> tuple[float, list[float], int]:
+    """``steps`` turns back to back, CUDA events around all of them (barrier and
+    sync on both sides), max over ranks; kernel durations sampled on every
+    ``steps // 25``-th turn (an event pair costs a turn a few microseconds, which
+    sampling every turn would charge to the whole-job number).
+    Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms, launches)."""
+    stride = max(1, steps // 25)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(0, steps, stride)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ranks.barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    start.record()
+    for i in range(steps):
+        n, _ = step(kev[i // stride] if i % stride == 0 else None)
+        launches += n
+    end.record()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    return ranks.max(start.elapsed_time(end)), [x.elapsed_time(y) for x, y in kev], launches
+
+
+def e2e_turns(worker, jobs, steps: int, ranks: Ranks) -> dict:
+    """The turn through the public worker API from host metadata, back to back.
+
+    Every step packs the descriptors and the block table on the host, copies
+    them from pinned memory, runs the table and load kernels and copies the
+    4-byte status word back; the status of a step is read on the host once
+    the next step is queued, and the last one before the timed region closes.
+    """
+    for _ in range(3):
+        worker.load(jobs)
+    ranks.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        worker.load(jobs, asynchronous=True)  # checks the previous step's status
+    worker.finish_pending()  # the last step's status, read on the host
+    e1.record()
+    torch.cuda.synchronize()
+    ranks.barrier()
+    return {"ms_per_step": ranks.max(e0.elapsed_time(e1)) / steps,
+            "h2d_bytes_per_step": int(worker.launcher.last_h2d), "d2h_bytes_per_step": 4}
+
+
+def worker_for(wl, cfg, layout, device, fp8):
+    """A ShiftWorker over the workload's caches, its stores adopted as sessions."""
     from marathon_b200.shift_store import ShiftStore
     from marathon_b200.worker import LoadJob, ShiftWorker
-    from marathon_b200.shift_kernels import RunSpec
+
+    names = [f"layer.{i}" for i in range(cfg.layers)]
+    store = ShiftStore(budget_tokens=sum(cfg.history), device=str(device))
+    for si, per_layer in enumerate(wl.stores):
+        store.adopt(f"s{si}", dict(zip(names, per_layer, strict=True)), 0, cfg.history[si])
+    worker = ShiftWorker(store, cfg.block_size, wl.inv_freq.cpu(), layout=layout, fp8=fp8,
+                         k_scales=wl.k_scales)
+    worker.register(dict(zip(names, wl.kv, strict=True)))
+    jobs = [LoadJob(f"s{si}", s.src_start, s.delta, s.dst_start, s.length,
+                    block_ids=wl.block_tables_host[si])
+            for si, segs in enumerate(cfg.segments) for s in segs]
+    return worker, jobs, names
+
+
+def roofline(rank_bytes: int, kernel_ms: list[float], traffic, kernel: str) -> dict:
+    peak, peak_kind = peaks()
+    mean = statistics.mean(kernel_ms)
+    achieved = rank_bytes / (mean / 1e3) / 1e9
+    return {
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+        "frac_of_8tbs": round(achieved / 8000.0, 4), "kernel": kernel,
+        "kernel_ms": round(mean, 4),
+        "kernel_ms_spans": "rope_tables_kernel + the load kernel (one event pair around "
+                           "both; the table kernel is ~0.3% of a c2 step)",
+        "kernel_samples": len(kernel_ms), "kernel_ms_best": round(min(kernel_ms), 4),
+        "kernel_ms_median": round(statistics.median(kernel_ms), 4),
+        "bytes_per_launch": rank_bytes,
+        "traffic": round(traffic) if traffic else None,
+    }
+
+
+def fp8_torch_check(wl) -> dict:
+    """Every layer of an e4m3 turn against a torch restatement on the GPU of
+    dequantise -> rotate -> requantise (fp32, the reference's tables as its GPU
+    path builds them, separate multiply and add kernels, divide by the layer's
+    K scale, saturate to +-448, round to e4m3): V bit-exact, K within one step."""
+    d = wl.cfg.head_size
+    worst = differ = total = 0
+    v_exact = True
+    for r in wl.runs:
+        bt = r.block_table.long()
+        pos = torch.arange(r.paged_start, r.paged_start + r.length, device=bt.device)
+        blk, off = bt[pos // wl.cfg.block_size], pos % wl.cfg.block_size
+        ang = float(r.delta) * wl.inv_freq
+        cos, sin = torch.cat((ang, ang)).cos(), torch.cat((ang, ang)).sin()
+        for li in range(wl.cfg.layers):
+            rows = wl.stores[r.session][li][r.store_start : r.store_start + r.length]
+            got = wl.kv[li][blk, off]
+            ks = wl.k_scales[li]
+            kf = rows[..., :d].float() * ks
+            turned = torch.cat((-kf[..., d // 2 :], kf[..., : d // 2]), dim=-1)
+            want = ((kf * cos + turned * sin) / ks).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+            def order(t):
+                u = t.view(torch.uint8).int()
+                return torch.where(u >= 128, 128 - u, u)
+
+            steps = (order(got[..., :d]) - order(want)).abs()
+            worst = max(worst, int(steps.max()))
+            differ += int((steps > 0).sum())
+            total += steps.numel()
+            v_exact &= bool(torch.equal(got[..., d:].view(torch.uint8),
+                                        rows[..., d:].view(torch.uint8)))
+    return {"k_max_steps": worst, "k_codes_one_step_off": differ, "k_codes": total,
+            "v_bit_exact": v_exact,
+            "reference": "torch fp32 dequantise -> rotate -> divide -> saturate -> e4m3 on "
+                         "the GPU, every layer"}
+
+
+def c3_extra(args, ranks: Ranks) -> dict:
+    """The FP8 turn (c3) on one GPU: the load kernel, the end-to-end call, the check."""
+    from marathon_b200.paged import KVLayers
+    from marathon_b200.shift_kernels import Launcher, set_load_kernel
+    from marathon_b200.workloads import build, config
+
+    cfg = config("c3")
+    wl = build(cfg, ranks.device, layout=args.layout)
+    wl.view = wl.store_view()
+    launcher = Launcher(KVLayers(wl.kv, cfg.block_size, args.layout, fp8=True))
+    load_step(launcher, wl, check=True)
+    for _ in range(args.warmup):
+        load_step(launcher, wl)
+    steps = max(args.steps, 10)
+    total_ms, kernel_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
+    ms = total_ms / steps
+    out = {"config": workload_config(cfg, 1, args.layout), "metric": METRIC,
+           "value": round(cfg.algorithmic_bytes() / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(ms, 4), "steps": steps, "target_ms": 0.781,
+           "roofline": roofline(wl.algorithmic_bytes(), kernel_ms,
+                                traffic_for(cfg.name, args.layout,
+                                            cfg.shifted_tokens * cfg.layers),
+                                "bulk_load_kernel (mshift_load, TMA)")}
+    prev = set_load_kernel("lsu")
+    try:
+        _, lsu_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), 10, ranks)
+    finally:
+        set_load_kernel(prev)
+    out["roofline"]["alternatives"] = {"lsu": {
+        "kernel": "move_kernel<load> (128-bit loads)",
+        "kernel_ms": round(statistics.mean(lsu_ms), 4),
+        "achieved": round(wl.algorithmic_bytes() / (statistics.mean(lsu_ms) / 1e3) / 1e9, 1)}}
+    worker, jobs, _ = worker_for(wl, cfg, args.layout, ranks.device, True)
+    e = e2e_turns(worker, jobs, max(10, min(args.steps, 100)), ranks)
+    out["e2e"] = {"value": round(cfg.algorithmic_bytes() / (e["ms_per_step"] / 1e3) / 1e9, 2),
+                  "unit": "GB/s", "ms_per_step": round(e["ms_per_step"], 4),
+                  "h2d_bytes_per_step": e["h2d_bytes_per_step"],
+                  "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+                  "api": "marathon_b200.worker.ShiftWorker.load"}
+    load_step(launcher, wl, check=True)
+    torch.cuda.synchronize()
+    out["check"] = fp8_torch_check(wl)
+    del worker, jobs, launcher, wl
+    torch.cuda.empty_cache()
+    return out
+
+
+def c4_extra(args, ranks: Ranks) -> dict:
+    """64 sessions (c4) in one launch per rank at TP ``world``, each rank its head shard."""
+    from marathon_b200.paged import KVLayers
+    from marathon_b200.sharding import head_shard
+    from marathon_b200.shift_kernels import Launcher
+    from marathon_b200.workloads import build, config
+
+    cfg = config("c4")
+    lo, hi = head_shard(cfg.heads, ranks.rank, ranks.world)
+    need = sum(cfg.history) * cfg.layers * cfg.bytes_per_token_layer(hi - lo)
+    free, _ = torch.cuda.mem_get_info(ranks.device)
+    if ranks.max(float(need > 0.9 * free)) > 0:  # one decision for every rank
+        return {"config": workload_config(cfg, ranks.world, args.layout),
+                "skipped": f"needs about {need / 1e9:.0f} GB per GPU at {hi - lo} heads"}
+    wl = build(cfg, ranks.device, head_lo=lo, head_hi=hi, layout=args.layout)
+    wl.view = wl.store_view()
+    launcher = Launcher(KVLayers(wl.kv, cfg.block_size, args.layout))
+    load_step(launcher, wl, check=True)
+    for _ in range(args.warmup):
+        load_step(launcher, wl)
+    steps = max(args.steps, 10)
+    total_ms, kernel_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
+    ms = total_ms / steps
+    out = {"config": workload_config(cfg, ranks.world, args.layout), "metric": METRIC,
+           "value": round(cfg.algorithmic_bytes() / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(ms, 4), "steps": steps, "runs": len(wl.runs),
+           "roofline": roofline(wl.algorithmic_bytes(), kernel_ms, None,
+                                "move_kernel<load> (mshift_load)")}
+    out["roofline"]["max_over_ranks_kernel_ms"] = round(ranks.max(statistics.mean(kernel_ms)), 4)
+    worker, jobs, _ = worker_for(wl, cfg, args.layout, ranks.device, False)
+    e = e2e_turns(worker, jobs, max(10, min(args.steps, 50)), ranks)
+    out["e2e"] = {"value": round(cfg.algorithmic_bytes() / (e["ms_per_step"] / 1e3) / 1e9, 2),
+                  "unit": "GB/s", "ms_per_step": round(e["ms_per_step"], 4),
+                  "h2d_bytes_per_step": e["h2d_bytes_per_step"],
+                  "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+                  "api": "marathon_b200.worker.ShiftWorker.load"}
+    del worker, jobs, launcher, wl
+    torch.cuda.empty_cache()
+    return out
+
+
+def native_arm(args) -> None:
+    from marathon_b200.paged import KVLayers
+    from marathon_b200.sharding import broadcast_table, head_shard, pack_table
+    from marathon_b200.shift_kernels import Launcher, RunSpec
     from marathon_b200.workloads import build, config, scaled
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=180))
-
+    ranks = Ranks()
+    device, rank, world = ranks.device, ranks.rank, ranks.world
     cfg = config(args.config)
     if args.layers:
         cfg = scaled(cfg, args.layers)
@@ -371,10 +747,10 @@ def native_arm(args) -> None:
                          f"{h_hi - h_lo} heads per rank, more than the GPU's "
                          f"{total / 1e9:.0f} GB (run it over more GPUs)")
     wl = build(cfg, device, head_lo=h_lo, head_hi=h_hi, layout=args.layout)
+    wl.view = wl.store_view()
     fp8 = cfg.dtype == "e4m3"
-    layers = KVLayers(wl.kv, cfg.block_size, args.layout, fp8=fp8)
-    launcher = Launcher(layers, tile_tokens=args.tile_tokens or None)
-    view = wl.store_view()
+    launcher = Launcher(KVLayers(wl.kv, cfg.block_size, args.layout, fp8=fp8),
+                        tile_tokens=args.tile_tokens or None)
 
     # control plane: the segment table is rank 0's, broadcast once over NCCL
     if world > 1:
@@ -383,20 +759,10 @@ def native_arm(args) -> None:
         if not torch.equal(mine, got.cpu()):
             raise SystemExit(f"rank {rank}: segment table differs from rank 0's")
 
-    def step(check=False, ev=None):
-        # the event pair brackets the table kernel and the load kernel together:
-        # an event between them would break the programmatic dependent launch
-        # that lets the load kernel's CTAs start while the table kernel ends
-        p = launcher.prepare_load(wl.runs, view, wl.inv_freq, k_scales=wl.k_scales)
-        if ev is not None:
-            ev[0].record()
-        n = launcher.launch(p)
-        if ev is not None:
-            ev[1].record()
-        launcher.finish(p, check)
-        return n, p.h2d_bytes
+    def step(ev=None):
+        return load_step(launcher, wl, ev)
 
-    step(check=True)  # first call: surface any rejected token before timing
+    load_step(launcher, wl, check=True)  # first call: surface any rejected token before timing
     clocks = Clocks(device)
     clocks.start()
     t_warm = time.perf_counter()
@@ -408,34 +774,8 @@ def native_arm(args) -> None:
         for _ in range(20):
             step()
         torch.cuda.synchronize()
-
-    # kernel durations are sampled on every `stride`-th step (at least 25
-    # samples): a timing-event pair costs the step a few microseconds, which
-    # per-step sampling would charge to every step of the whole-job number
-    stride = max(1, args.steps // 25)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(0, args.steps, stride)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier(device_ids=[local])
-    torch.cuda.synchronize()
-    launches = 0
-    start.record()
-    for i in range(args.steps):
-        n, _ = step(ev=kev[i // stride] if i % stride == 0 else None)
-        launches += n
-    end.record()
-    torch.cuda.synchronize()
+    max_ms, per_step, launches = timed_turns(step, args.steps, ranks)
     clk = clocks.stop()
-    if world > 1:
-        dist.barrier(device_ids=[local])
-    elapsed = start.elapsed_time(end)
-    per_step = [a.elapsed_time(b) for a, b in kev]
-    kernel_ms = statistics.mean(per_step)
-    t = torch.tensor([elapsed], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
     turn_bytes = cfg.algorithmic_bytes()  # the whole turn, all heads, all ranks
     rank_bytes = wl.algorithmic_bytes()
     ms_per_step = max_ms / args.steps
@@ -448,17 +788,13 @@ def native_arm(args) -> None:
 
         prev = set_load_kernel("lsu" if fp8 else "bulk")  # the one auto did not pick
         try:
-            aev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(max(10, min(args.steps, 100)))]
-            step(check=True)
-            for a_, b_ in aev:
-                step(ev=(a_, b_))
-            torch.cuda.synchronize()
-            a_ms = statistics.mean(a_.elapsed_time(b_) for a_, b_ in aev)
+            load_step(launcher, wl, check=True)
+            _, a_ms, _ = timed_turns(step, max(10, min(args.steps, 100)), ranks)
             name = ("lsu", "move_kernel<load> (128-bit loads)") if fp8 else (
                 "bulk", "bulk_load_kernel (TMA cp.async.bulk, mbarrier ring)")
-            alt = {name[0]: {"kernel": name[1], "kernel_ms": round(a_ms, 4),
-                             "achieved": round(rank_bytes / (a_ms / 1e3) / 1e9, 1)}}
+            m = statistics.mean(a_ms)
+            alt = {name[0]: {"kernel": name[1], "kernel_ms": round(m, 4),
+                             "achieved": round(rank_bytes / (m / 1e3) / 1e9, 1)}}
         finally:
             set_load_kernel(prev)
 
@@ -467,13 +803,13 @@ def native_arm(args) -> None:
     if not args.no_save:
         sruns = [RunSpec(r.session, r.store_start, r.length, block_table=r.block_table,
                          paged_start=r.paged_start) for r in wl.runs]
-        sp = launcher.prepare_save(sruns, view)
+        sp = launcher.prepare_save(sruns, wl.view)
         launcher.launch(sp)
         launcher.finish(sp, True)
         sev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(max(10, min(args.steps, 100)))]
         for a, b in sev:
-            sp = launcher.prepare_save(sruns, view)
+            sp = launcher.prepare_save(sruns, wl.view)
             a.record()
             launcher.launch(sp)
             b.record()
@@ -485,55 +821,48 @@ def native_arm(args) -> None:
 
     # end to end through the public worker API, from host metadata
     e2e = None
-    if not args.no_e2e:
-        names = [f"layer.{i}" for i in range(cfg.layers)]
-        store = ShiftStore(budget_tokens=sum(cfg.history), device=str(device))
-        for si, per_layer in enumerate(wl.stores):
-            store.adopt(f"s{si}", dict(zip(names, per_layer, strict=True)), 0, cfg.history[si])
-        worker = ShiftWorker(store, cfg.block_size, wl.inv_freq.cpu(), layout=args.layout,
-                             fp8=fp8, k_scales=wl.k_scales)
-        worker.register(dict(zip(names, wl.kv, strict=True)))
-        jobs = [LoadJob(f"s{si}", s.src_start, s.delta, s.dst_start, s.length,
-                        block_ids=wl.block_tables_host[si])
-                for si, segs in enumerate(cfg.segments) for s in segs]
-        for _ in range(3):
-            worker.load(jobs)
-        e_steps = max(10, min(args.steps, 100))
-        if world > 1:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        h2d = 0
-        for _ in range(e_steps):
-            worker.load(jobs, check=True)  # packs, copies, launches, reads the status back
-            h2d = worker.launcher.last_h2d
-        e1.record()
-        torch.cuda.synchronize()
-        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
-        if world > 1:
-            dist.all_reduce(et, op=dist.ReduceOp.MAX)
-        e_ms = float(et.item()) / e_steps
-        e2e = {"value": round(turn_bytes / (e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-               "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": 4, "api": "marathon_b200.worker.ShiftWorker.load"}
-
     host_tier = None
-    if world == 1 and not args.no_host_tier and not args.no_e2e:
-        host_tier = host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device)
+    if not args.no_e2e:
+        worker, jobs, names = worker_for(wl, cfg, args.layout, device, fp8)
+        e = e2e_turns(worker, jobs, max(10, min(args.steps, 100)), ranks)
+        e2e = {"value": round(turn_bytes / (e["ms_per_step"] / 1e3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(e["ms_per_step"], 4),
+               "h2d_bytes_per_step": e["h2d_bytes_per_step"],
+               "d2h_bytes_per_step": e["d2h_bytes_per_step"],
+               "api": "marathon_b200.worker.ShiftWorker.load",
+               "status_read": "each step's 4-byte status is copied back every step and read "
+                              "on the host once the next step is queued; the last inside "
+                              "the timed region"}
+        if world == 1 and not args.no_host_tier:
+            host_tier = host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device)
+        del worker, jobs
 
-    peak, peak_kind = peaks()
-    achieved = rank_bytes / (kernel_ms / 1e3) / 1e9
     units = cfg.shifted_tokens * cfg.layers  # (token, layer) units of the whole turn
     traffic = traffic_for(cfg.name, args.layout, units)
     if traffic is not None:
         traffic *= (h_hi - h_lo) / cfg.heads  # this rank's head shard of each unit
+    roof = roofline(rank_bytes, per_step, traffic,
+                    "bulk_load_kernel (mshift_load, TMA)" if fp8
+                    else "move_kernel<load> (mshift_load)")
+    roof["alternatives"] = alt
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        s = CpuPath(cfg).sample(args.cpu_seconds)
-        cpu = {"value": round(s["gbs"], 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
-               "kind": "port", "sample": s["sample"],
-               "ms_per_turn_extrapolated": round(s["ms_per_layer"] * cfg.layers, 1)}
+        base = CpuPath(cfg)
+        smp = base.sample(args.cpu_seconds)
+        cpu = {"value": round(smp["gbs"], 3), "unit": "GB/s", "cores": base.threads,
+               "kind": base.kind, "impl": base.impl, "sample": smp["sample"],
+               "ms_per_turn_extrapolated": round(smp["ms_per_layer"] * cfg.layers, 1)}
+        del base
+    tile_tokens = launcher.tile_tokens
+    del launcher, wl
+    torch.cuda.empty_cache()
+
+    extra = {}
+    if not args.no_extra and args.config == "c2" and not args.layers:
+        if world == 1:
+            extra["c3"] = c3_extra(args, ranks)
+        else:
+            extra["c4"] = c4_extra(args, ranks)
 
     if rank == 0:
         line = {
@@ -549,44 +878,20 @@ def native_arm(args) -> None:
             "vs_baseline": None,
             "dtype": "e4m3" if fp8 else "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": f"{cfg.name} {cfg.model} shift turn",
-                "layers": cfg.layers, "tokens_shifted": cfg.shifted_tokens,
-                "deltas": sorted({s.delta for segs in cfg.segments for s in segs}),
-                "heads": cfg.heads, "heads_per_rank": h_hi - h_lo, "head_size": cfg.head_size,
-                "block_size": cfg.block_size, "layout": args.layout, "parallelism":
-                f"kv-head shard tp{world}", "turn_bytes": turn_bytes,
-                "gib_s": round(turn_bytes / (ms_per_step / 1e3) / 2**30, 2),
-                "l2": "inputs larger than L2 (store + paged cache per step >> 126 MB)",
-                "tile_tokens": launcher.tile_tokens,
-            },
-            "roofline": {
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "frac_of_8tbs": round(achieved / 8000.0, 4),
-                "kernel": ("bulk_load_kernel (mshift_load, TMA)" if fp8
-                           else "move_kernel<load> (mshift_load)"),
-                "kernel_ms": round(kernel_ms, 4),
-                "kernel_ms_spans": "rope_tables_kernel + the load kernel (one event pair "
-                                   "around both; the table kernel is ~0.3% of a c2 step)",
-                "kernel_samples": len(per_step),
-                "kernel_ms_best": round(min(per_step), 4),
-                "kernel_ms_median": round(statistics.median(per_step), 4),
-                "bytes_per_launch": rank_bytes,
-                "traffic": round(traffic) if traffic else None,
-                "alternatives": alt,
-            },
+            "config": workload_config(cfg, world, args.layout),
+            "gib_s": round(turn_bytes / (ms_per_step / 1e3) / 2**30, 2),
+            "launch": {"tile_tokens": tile_tokens},
+            "roofline": roof,
             "e2e": e2e,
             "save": save,
             "host_tier": host_tier,
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,
+            **extra,
         }
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier(device_ids=[local])
-        dist.destroy_process_group()
+    ranks.close()
 
 
 def main() -> None:

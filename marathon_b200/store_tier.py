@@ -143,6 +143,9 @@ class StagedLoad:
     last: torch.cuda.Event
     errs: torch.Tensor
     n_chunks: int
+    #: queued on the caller's own stream (a device store): work queued there
+    #: later is ordered after it without waiting on the host
+    same_stream: bool = False
 
     def wait_layer(self, layer: int, stream=None) -> None:
         (stream or torch.cuda.current_stream()).wait_event(self.layer_done[layer])

@@ -147,13 +147,28 @@ class ShiftWorker:
         the mover's own streams (``wait_layer`` orders a layer's consumers
         after its rows); a device store's load is queued on the current
         stream, so later work on that stream is ordered after it anyway and
-        only the host-side status check is deferred.
+        only the host-side status check is deferred -- to ``finish_pending``
+        or to the next asynchronous ``load``, which packs and queues its own
+        batch first, so a caller issuing loads back to back keeps the GPU busy
+        while the host prepares the next one.
         """
         if not jobs:
             return []
         if self.launcher is None:
             raise ShiftError("no KV caches registered")
-        self.finish_pending()
+        prev = None
+        if (asynchronous and self.mover is None and self.pending is not None
+                and self.pending.same_stream):
+            prev, self.pending = self.pending, None  # checked once this batch is queued
+        else:
+            self.finish_pending()
+        try:
+            return self._load(jobs, check, asynchronous)
+        finally:
+            if prev is not None:
+                prev.check()
+
+    def _load(self, jobs: list[LoadJob], check: bool, asynchronous: bool) -> list[LoadJob]:
         names = self.layers.names
         name_set = self._name_set
         accepted: list[LoadJob] = []
@@ -196,7 +211,7 @@ class ShiftWorker:
         la.finish(p, False)
         done = torch.cuda.Event()
         done.record(p.stream)
-        return StagedLoad([done] * len(self.layers), done, errs, 1)
+        return StagedLoad([done] * len(self.layers), done, errs, 1, same_stream=True)
 
     def wait_layer(self, name: str) -> None:
         """Order the current stream after layer ``name`` of a pending staged load."""
