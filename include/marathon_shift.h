@@ -15,7 +15,11 @@
  *     table index inside a run descriptor) skip that token and OR an
  *     MSHIFT_EBIT_* bit into *err, which the caller zeroes beforehand and reads
  *     after the stream has synchronised.  No kernel traps or faults on a bad
- *     descriptor.
+ *     descriptor.  While a batched load or save runs, bits 8..31 of *err
+ *     count the tiles its CTAs have claimed (they are cleared again before the
+ *     launch completes), so one status word must not be shared by launches
+ *     that can run at the same time; launches ordered on one stream may share
+ *     it and accumulate their flags.
  *
  * Layout vocabulary (shared with the Python package marathon_b200):
  *   store    one buffer per (session, layer): [capacity, heads, 2*head_size],

@@ -260,6 +260,9 @@ struct KArgs {
   // diagnostic hook of the TMA load kernel: 0 = normal; n > 0 bounds every
   // consumer warp's first full-barrier wait to n - 1 rounds
   uint32_t first_wait;
+  // 1: CTAs claim tiles from a counter kept in bits 8..31 of *err (see
+  // claim_tile); 0: CTA b takes tiles b, b + grid, b + 2*grid, ...
+  int32_t dyn;
   // single run, single layer (runs == nullptr)
   mshift_run run0;
   void* store0;
@@ -288,12 +291,31 @@ __device__ __forceinline__ void allow_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Dynamic tile scheduling.  The caller zeroes the status word *err before
+// the launch; its low 8 bits collect MSHIFT_EBIT_* flags and its high 24 bits
+// count claimed tiles.  Every claim adds 256 and returns the tile index; each
+// CTA claims until it draws an index >= total, so exactly total + gridDim.x
+// claims are made and the one that draws total + gridDim.x - 1 is the last
+// claim of the launch: it clears the counter bits, leaving only the flags
+// (the caller reads *err after the launch exactly as with static tiles).
+// Tiles then go to whichever CTA is free first, so a launch ends within one
+// tile of its fastest CTA instead of after its slowest stride.
+__device__ __forceinline__ int claim_tile(uint32_t* err, int total) {
+  const uint32_t old = atomicAdd(err, 256u);
+  const int t = static_cast<int>(old >> 8);
+  if (t == total + static_cast<int>(gridDim.x) - 1) atomicAnd(err, 0xFFu);
+  return t;
+}
+
 // One templated kernel for both directions.
 //   SAVE = false: store rows -> paged cache, K rotated (load)
 //   SAVE = true : paged cache -> store rows, bit copy (save)
 template <class E, int D, int ROT, bool SAVE>
 __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const KArgs a) {
   wait_prior_grid();
+  // the next turn's table kernel may launch now: it computes its tables while
+  // this launch runs and waits for this launch to complete before it ends
+  allow_dependents();
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;      // 16-byte vectors per K (or V) row
@@ -308,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
   __shared__ int64_t s_off[kMaxTile];
   __shared__ __align__(16) float s_cs[HALF > 0 ? HALF : 4];
   __shared__ __align__(16) float s_sn[HALF > 0 ? HALF : 4];
+  __shared__ int s_next;  // the tile claimed for this CTA's next iteration
 
   const int g = threadIdx.x % G;
   const int u_first = threadIdx.x / G;
@@ -317,7 +340,16 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
   const int kb = g < NP ? g + NP : g + G;
   const int total = a.tiles_per_layer * a.n_layers;
 
-  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+  int w = blockIdx.x;
+  if (a.dyn) {
+    if (threadIdx.x == 0) s_next = claim_tile(a.err, total);
+    __syncthreads();
+    w = s_next;
+  }
+  // the next tile is claimed while this one is processed; s_next is written
+  // between the tile's two barriers and read after the second, and every
+  // thread has read it before the next iteration's first barrier
+  for (; w < total; w = a.dyn ? s_next : w + static_cast<int>(gridDim.x)) {
     const int layer = w / a.tiles_per_layer;
     const int tile = w - layer * a.tiles_per_layer;
 
@@ -363,8 +395,11 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
     const int nt = min(a.tile_tokens, run.len - t0);
     const bool tile_ok = ok_desc && nt > 0 && t0 >= 0;
 
-    __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn
-    if (threadIdx.x == 0 && bits) atomicOr(a.err, bits);
+    __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn / s_next
+    if (threadIdx.x == 0) {
+      if (bits) atomicOr(a.err, bits);
+      if (a.dyn) s_next = claim_tile(a.err, total);
+    }
     if (tile_ok) {
       for (int t = threadIdx.x; t < nt; t += kThreads) {
         const int64_t spos = run.store_start + t0 + t;
@@ -872,12 +907,18 @@ __global__ void rope_tables_kernel(const int64_t* deltas, int32_t n, const float
                                    int32_t half, float* out) {
   allow_dependents();  // the load kernel may launch; it waits for our writes
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)n * half) return;
-  const int64_t d = i / half;
-  const int64_t j = i - d * half;
-  const float ang = __fmul_rn(static_cast<float>(deltas[d]), inv_freq[j]);
-  out[d * 2 * half + j] = cosf(ang);
-  out[d * 2 * half + half + j] = sinf(ang);
+  if (i < (int64_t)n * half) {
+    const int64_t d = i / half;
+    const int64_t j = i - d * half;
+    const float ang = __fmul_rn(static_cast<float>(deltas[d]), inv_freq[j]);
+    out[d * 2 * half + j] = cosf(ang);
+    out[d * 2 * half + half + j] = sinf(ang);
+  }
+  // Launched as a programmatic dependent of the previous turn's load kernel,
+  // this grid may run alongside it; it reads nothing that kernel writes, but
+  // it must not complete before it, so that the next load kernel -- which
+  // waits for this grid -- is ordered after the previous one too.
+  wait_prior_grid();
 }
 
 // ------------------------------------------------------------------ dispatch
@@ -1000,12 +1041,15 @@ cudaError_t launch_dependent(void (*fn)(Params...), dim3 grid, dim3 block, size_
   return cudaLaunchKernelEx(&cfg, fn, args...);
 }
 
-int launch(KernelFn fn, int slot, const KArgs& args, cudaStream_t stream, bool pdl = false) {
+int launch(KernelFn fn, int slot, KArgs args, cudaStream_t stream, bool pdl = false) {
   const int64_t total = (int64_t)args.tiles_per_layer * args.n_layers;
   if (total <= 0) return MSHIFT_OK;
   int grid = 0;
   int st = grid_for(fn, slot, total, &grid);
   if (st != MSHIFT_OK) return st;
+  // batched launches claim tiles dynamically while the claim counter fits
+  // bits 8..31 of the status word
+  args.dyn = (args.runs != nullptr && total + grid < (int64_t{1} << 24)) ? 1 : 0;
   cudaError_t e;
   if (pdl) {
     e = launch_dependent(fn, dim3(grid), dim3(kThreads), 0, stream, args);
@@ -1154,9 +1198,9 @@ int mshift_rope_tables(const int64_t* deltas, int32_t n, const float* inv_freq, 
   const int threads = 128;
   const int64_t blocks = (total + threads - 1) / threads;
   if (blocks > INT32_MAX) return MSHIFT_EINVAL;
-  rope_tables_kernel<<<static_cast<unsigned>(blocks), threads, 0,
-                       static_cast<cudaStream_t>(stream)>>>(deltas, n, inv_freq, half, tables);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_dependent(rope_tables_kernel, dim3(static_cast<unsigned>(blocks)),
+                                         dim3(threads), 0, static_cast<cudaStream_t>(stream),
+                                         deltas, n, inv_freq, half, tables);
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
 }
 

@@ -758,7 +758,10 @@ class Launcher:
         word, or into the device word at address ``err`` when given (a word
         the caller shares between several launches and reads once).
         """
-        if p.uploaded is not None:
+        # a descriptor copy that has already completed needs no stream wait;
+        # leaving it out keeps this batch's kernels directly behind the
+        # previous batch's in the stream (programmatic dependent launch)
+        if p.uploaded is not None and not p.uploaded.query():
             p.stream.wait_event(p.uploaded)
         stream = p.stream.cuda_stream
         err_ptr = p.base if err is None else int(err)
