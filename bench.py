@@ -494,6 +494,15 @@ class Ranks:
             self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def gather(self, values: list[float]) -> list[list[float]]:
+        """Every rank's ``values`` (same length on every rank), in rank order."""
+        t = torch.tensor(values, dtype=torch.float64, device=self.device)
+        if self.world == 1:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
     def close(self):
         if self.world > 1:
             self.barrier()
@@ -517,12 +526,14 @@ def load_step(launcher, wl, ev=None, check=False) -> tuple[int, int]:
     return n, p.h2d_bytes
 
 
-def timed_turns(step, steps: int, ranks: Ranks) -> tuple[float, list[float], int]:
+def timed_turns(step, steps: int, ranks: Ranks, detail: dict | None = None):
     """``steps`` turns back to back, CUDA events around all of them (barrier and
     sync on both sides), max over ranks; kernel durations sampled on every
     ``steps // 25``-th turn (an event pair costs a turn a few microseconds, which
     sampling every turn would charge to the whole-job number).
-    Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms, launches)."""
+    Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms,
+    launches); with ``detail``, also every rank's device ms per turn, mean
+    sampled kernel ms and host (issuing) ms per turn."""
     stride = max(1, steps // 25)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(0, steps, stride)]
@@ -530,14 +541,23 @@ def timed_turns(step, steps: int, ranks: Ranks) -> tuple[float, list[float], int
     ranks.barrier()
     torch.cuda.synchronize()
     launches = 0
+    t0 = time.perf_counter()
     start.record()
     for i in range(steps):
         n, _ = step(kev[i // stride] if i % stride == 0 else None)
         launches += n
     end.record()
+    host_ms = (time.perf_counter() - t0) * 1e3
     torch.cuda.synchronize()
     ranks.barrier()
-    return ranks.max(start.elapsed_time(end)), [x.elapsed_time(y) for x, y in kev], launches
+    mine = start.elapsed_time(end)
+    kernel = [x.elapsed_time(y) for x, y in kev]
+    if detail is not None:
+        rows = ranks.gather([mine / steps, statistics.mean(kernel), host_ms / steps])
+        detail.update({"ms_per_step": [round(r[0], 4) for r in rows],
+                       "kernel_ms": [round(r[1], 4) for r in rows],
+                       "host_issue_ms_per_step": [round(r[2], 4) for r in rows]})
+    return ranks.max(mine), kernel, launches
 
 
 def e2e_turns(worker, jobs, steps: int, ranks: Ranks) -> dict:
@@ -774,7 +794,8 @@ def native_arm(args) -> None:
         for _ in range(20):
             step()
         torch.cuda.synchronize()
-    max_ms, per_step, launches = timed_turns(step, args.steps, ranks)
+    per_rank: dict = {}
+    max_ms, per_step, launches = timed_turns(step, args.steps, ranks, per_rank)
     clk = clocks.stop()
     turn_bytes = cfg.algorithmic_bytes()  # the whole turn, all heads, all ranks
     rank_bytes = wl.algorithmic_bytes()
@@ -888,6 +909,7 @@ def native_arm(args) -> None:
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "clocks": clk,
+            "per_rank": per_rank if world > 1 else None,
             **extra,
         }
         print(json.dumps(line), flush=True)
