@@ -643,6 +643,10 @@ struct BulkMeta {
 #ifndef MSHIFT_BULK_MIN_BLOCKS
 #define MSHIFT_BULK_MIN_BLOCKS 2
 #endif
+#ifndef MSHIFT_BULK_UNITS_E4M3
+#define MSHIFT_BULK_UNITS_E4M3 1
+#endif
+constexpr int kBulkUnitsE4m3 = MSHIFT_BULK_UNITS_E4M3;
 constexpr int kBulkConsumerWarps = MSHIFT_BULK_CONSUMER_WARPS;  // warps that rotate and store
 constexpr int kBulkConsumers = kBulkConsumerWarps * 32;
 constexpr int kBulkThreads = kBulkConsumers + 32;              // + one producer warp
@@ -821,9 +825,10 @@ __global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_loa
   }
 
   // -------------------------------------------------------------- consumers
-  // e4m3 units are arithmetic-heavy: one unit in flight per thread, and the
-  // thread's cos/sin slice held in registers for the whole stage.
-  constexpr int U = E::kScaled ? 1 : 2;
+  // e4m3 units carry twice the elements per byte: one unit in flight per
+  // thread (MSHIFT_BULK_UNITS_E4M3 overrides), and the thread's cos/sin slice
+  // held in registers for the whole stage.
+  constexpr int U = E::kScaled ? kBulkUnitsE4m3 : 2;
   constexpr bool kRegTable = E::kScaled;
   const int g = threadIdx.x % G;
   const int u_first = threadIdx.x / G;

@@ -507,42 +507,52 @@ class MarathonShiftConnector(KVConnectorBase_V1):
         meta.saves.append(_Save(session or "", lo, hi - lo, list(blocks), self._bs))
 
     def build_connector_meta(self, scheduler_output: SchedulerOutput):
+        """The loads and saves of one scheduler step.
+
+        A newly scheduled request brings its block table, its extent releases
+        and (when ``get_num_new_matched_tokens`` planned a match) its loads; a
+        running request may bring more blocks.  Either way the positions the
+        step computes are its save candidates, planned in scheduling order --
+        the order the worker replays them in, so both stores touch and evict
+        sessions alike.
+        """
         meta = ShiftConnectorMetadata()
+        computing: list[tuple[str, int]] = []  # (request, first position computed)
         for req in scheduler_output.scheduled_new_reqs:
-            rid = req.req_id
-            self._blocks[rid] = list(req.block_ids[0])
-            session = self._table.session_of(rid) or ""
-            if self._extents and session:
-                for g, p0, n in (self._params.get(rid) or {}).get("release", ()):
-                    self._store.release(session, int(g), int(p0), int(n))
-                    meta.releases.append((session, int(g), int(p0), int(n)))
-            if rid in self._need_load and rid in self._multi:
-                table = list(self._blocks[rid])  # one block table shared by the segments
-                for seg in self._multi[rid]:
-                    n = seg["dst_end"] - seg["dst_start"]
-                    meta.loads.append(_Load(session, seg["dst_start"] - seg["delta"],
-                                            seg["delta"], seg["dst_start"], n, table, self._bs,
-                                            seg.get("gen", -1)))
-                self._need_load.discard(rid)
-            elif rid in self._need_load:
-                lo, hi, delta, gen = self._plans[rid]
-                meta.loads.append(_Load(session, lo - delta, delta, lo, hi - lo,
-                                        list(self._blocks[rid]), self._bs, gen))
-                self._need_load.discard(rid)
-            lo = req.num_computed_tokens
-            self._plan_save(meta, rid, lo, lo + scheduler_output.num_scheduled_tokens[rid])
-
+            self._blocks[req.req_id] = list(req.block_ids[0])
+            self._admit(meta, req.req_id)
+            computing.append((req.req_id, req.num_computed_tokens))
         cached = scheduler_output.scheduled_cached_reqs
-        for i, rid in enumerate(cached.req_ids):
-            new_blocks = cached.new_block_ids[i]
-            if new_blocks is not None:
-                self._blocks.setdefault(rid, []).extend(new_blocks[0])
-            lo = cached.num_computed_tokens[i]
+        for rid, more, done in zip(cached.req_ids, cached.new_block_ids,
+                                   cached.num_computed_tokens, strict=True):
+            if more is not None:
+                self._blocks.setdefault(rid, []).extend(more[0])
+            computing.append((rid, done))
+        for rid, lo in computing:
             self._plan_save(meta, rid, lo, lo + scheduler_output.num_scheduled_tokens[rid])
-
         for rid in scheduler_output.finished_req_ids:
             self._forget(rid)
         return meta
+
+    def _admit(self, meta: ShiftConnectorMetadata, rid: str) -> None:
+        """A request's first scheduled step: its releases and the loads planned for it."""
+        session = self._table.session_of(rid) or ""
+        if self._extents and session:
+            for g, p0, n in (self._params.get(rid) or {}).get("release", ()):
+                self._store.release(session, int(g), int(p0), int(n))
+                meta.releases.append((session, int(g), int(p0), int(n)))
+        if rid not in self._need_load:
+            return
+        self._need_load.discard(rid)
+        table = self._blocks[rid]  # one block table, shared by all the request's segments
+        if rid in self._multi:
+            segments = [(s["dst_start"], s["dst_end"], s["delta"], s.get("gen", -1))
+                        for s in self._multi[rid]]
+        else:
+            segments = [self._plans[rid]]
+        for lo, hi, delta, gen in segments:
+            meta.loads.append(_Load(session, lo - delta, delta, lo, hi - lo, list(table),
+                                    self._bs, gen))
 
     def update_connector_output(self, connector_output) -> None:
         """Scheduler side: apply the workers' failed saves to the mirror store."""
@@ -557,12 +567,11 @@ class MarathonShiftConnector(KVConnectorBase_V1):
             self._store.release(session, gen, pos0, n)
 
     def _forget(self, rid: str) -> None:
-        self._gap.release(rid)
-        self._multi.pop(rid, None)
-        self._blocks.pop(rid, None)
-        self._params.pop(rid, None)
-        self._plans.pop(rid, None)
+        """Drop everything held for a finished request (idempotent)."""
+        for held in (self._multi, self._blocks, self._params, self._plans):
+            held.pop(rid, None)
         self._need_load.discard(rid)
+        self._gap.release(rid)
         self._table.release(rid)
 
     def request_finished(self, request: Request, block_ids: list[int]):
