@@ -47,13 +47,12 @@
 #include "../../include/marathon_shift.h"
 
 // Tuning knobs (compile-time; the defaults are the measured best on B200):
-//   MSHIFT_MIN_BLOCKS  resident CTAs per SM requested from ptxas (register cap:
-//                      2 keeps the load kernel at <= 128 registers, two CTAs per SM)
+//   MSHIFT_MIN_BLOCKS  resident CTAs per SM requested from ptxas (register cap)
 //   MSHIFT_UNITS       (token, head) units each thread keeps in flight
 //   MSHIFT_LOAD_HINT   0: ld.global.cs  1: ld.global.nc  2: ld.global.nc.L1::no_allocate.L2::256B
 //   MSHIFT_STORE_HINT  0: st.global.cs  1: st.global (write-back)
 #ifndef MSHIFT_MIN_BLOCKS
-#define MSHIFT_MIN_BLOCKS 2
+#define MSHIFT_MIN_BLOCKS 1
 #endif
 #ifndef MSHIFT_UNITS
 #define MSHIFT_UNITS 2
@@ -308,133 +307,9 @@ __device__ __forceinline__ int claim_tile(uint32_t* err, int total) {
   return t;
 }
 
-// A tile as the unit loop sees it: where its rows are, how many tokens, and
-// whether K is rotated.  Identical in every thread of the CTA.
-struct TileMove {
-  char* store;    // session buffer of the tile's layer
-  char* kbase;    // paged cache K / V bases of the layer
-  char* vbase;
-  int64_t row0;   // store row of the tile's first token
-  int nt;         // tokens in the tile
-  bool ok;        // descriptors valid and the tile non-empty
-  bool rot;       // the run has a rotation table (loads only)
-};
-
-// What the slot lookup of a tile's tokens needs, plus the tile's move view.
-struct TilePlan {
-  TileMove m;
-  const int64_t* slots;        // run's explicit slots (or null: block-table mode)
-  const int32_t* block_table;
-  int64_t paged_start;         // logical position of the tile's first token
-  int64_t cap;                 // session capacity (store bounds check)
-  int32_t block_table_len;
-  const float* tab;            // the run's rotation table row (loads)
-  uint32_t bits;               // descriptor errors, ORed once per tile
-};
-
-// Resolve tile w of a launch from the run descriptors (uniform across the CTA).
-template <int HALF, bool SAVE>
-__device__ __forceinline__ TilePlan plan_tile(const KArgs& a, int w) {
-  TilePlan p;
-  const int layer = w / a.tiles_per_layer;
-  const int tile = w - layer * a.tiles_per_layer;
-  mshift_run run;
-  bool ok_desc = true;
-  p.bits = 0;
-  p.tab = nullptr;
-  if (a.runs != nullptr) {
-    int lo = 0, hi = a.n_runs - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
-    }
-    run = a.runs[lo];
-    const bool sess = run.session >= 0 && run.session < a.n_sessions;
-    p.m.store = sess ? static_cast<char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
-                     : nullptr;
-    p.cap = sess ? a.store_caps[run.session] : 0;
-    if (!sess || p.m.store == nullptr || !aligned16(p.m.store)) {
-      ok_desc = false;
-      p.bits |= MSHIFT_EBIT_SESSION;
-    }
-    p.m.kbase = static_cast<char*>(a.k_ptrs[layer]);
-    p.m.vbase = static_cast<char*>(a.v_ptrs[layer]);
-    if (!SAVE) {
-      if (run.table >= 0 && run.table < a.n_tables) p.tab = a.tables + (int64_t)run.table * 2 * HALF;
-      else if (run.table != -1) { ok_desc = false; p.bits |= MSHIFT_EBIT_TABLE; }
-    }
-  } else {
-    run = a.run0;
-    p.m.store = static_cast<char*>(a.store0);
-    p.cap = a.cap0;
-    p.m.kbase = static_cast<char*>(a.k0);
-    p.m.vbase = static_cast<char*>(a.v0);
-    p.tab = SAVE ? nullptr : a.table0;
-  }
-  if (p.m.kbase == nullptr || p.m.vbase == nullptr || !aligned16(p.m.kbase) ||
-      !aligned16(p.m.vbase)) {
-    ok_desc = false;
-    p.bits |= MSHIFT_EBIT_SLOT;
-  }
-  const int t0 = (tile - run.tile_begin) * a.tile_tokens;
-  p.m.nt = min(a.tile_tokens, run.len - t0);
-  p.m.ok = ok_desc && p.m.nt > 0 && t0 >= 0;
-  p.m.row0 = run.store_start + t0;
-  p.m.rot = !SAVE && HALF > 0 && p.tab != nullptr;
-  p.slots = run.slots != nullptr ? run.slots + t0 : nullptr;
-  p.block_table = run.block_table;
-  p.block_table_len = run.block_table_len;
-  p.paged_start = run.paged_start + t0;
-  return p;
-}
-
-// One token's slot lookup in two halves, so the global load of the block-table
-// entry can be issued before the previous tile is moved and used after it.
-struct TokenSlot {
-  int64_t raw;   // block-table entry (block-table mode) or the slot itself
-  int32_t off;   // position within its block (block-table mode)
-  bool found;    // the block-table index was in range
-};
-
-__device__ __forceinline__ TokenSlot fetch_slot(const KArgs& a, const TilePlan& p, int t) {
-  TokenSlot s;
-  s.off = 0;
-  if (p.slots != nullptr) {
-    s.raw = p.slots[t];
-    s.found = true;
-  } else {
-    const int64_t pos = p.paged_start + t;
-    const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
-    s.found = bi >= 0 && bi < p.block_table_len;
-    s.raw = s.found ? static_cast<int64_t>(p.block_table[bi]) : 0;
-    s.off = s.found ? static_cast<int32_t>(pos % a.block_size) : 0;
-  }
-  return s;
-}
-
-// The token's element offset in the paged cache, or -1 (its error bits ORed).
-__device__ __forceinline__ int64_t finish_slot(const KArgs& a, const TilePlan& p, int t,
-                                               const TokenSlot& s) {
-  const int64_t slot = p.slots != nullptr ? s.raw : s.raw * a.block_size + s.off;
-  const bool slot_ok = s.found && slot >= 0 && slot < a.num_slots;
-  const int64_t spos = p.m.row0 + t;
-  const bool store_ok = spos >= 0 && spos < p.cap;
-  if (!slot_ok || !store_ok)
-    atomicOr(a.err, (slot_ok ? 0u : MSHIFT_EBIT_SLOT) | (store_ok ? 0u : MSHIFT_EBIT_STORE));
-  return (slot_ok && store_ok)
-             ? (slot / a.block_size) * a.blk_stride + (slot % a.block_size) * a.off_stride
-             : -1;
-}
-
 // One templated kernel for both directions.
 //   SAVE = false: store rows -> paged cache, K rotated (load)
 //   SAVE = true : paged cache -> store rows, bit copy (save)
-//
-// Tiles are software-pipelined: while a CTA moves tile i it already holds the
-// index of tile i + 1, has issued the global loads of that tile's block-table
-// entries and table row, and writes its paged offsets into the other half of
-// a double-buffered shared array after moving tile i.  One barrier per tile
-// then separates the two; no CTA waits for a slot lookup between tiles.
 template <class E, int D, int ROT, bool SAVE>
 __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const KArgs a) {
   wait_prior_grid();
@@ -448,16 +323,14 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
   constexpr int NP = HALF / VEC;   // rotating partner pairs per row
   constexpr int G = NV / 2;        // threads per (token, head) unit
   constexpr int UPP = kThreads / G;
-  constexpr int TH = HALF > 0 ? HALF : 4;
   static_assert(D % (2 * VEC) == 0, "head_size must hold an even number of 16-byte vectors");
   static_assert(HALF % VEC == 0 && NP <= G, "rotary half must be whole vectors");
   static_assert(kThreads % G == 0, "threads per unit must divide the CTA");
-  static_assert(kMaxTile <= kThreads && HALF <= kThreads, "one thread per token / table entry");
 
-  __shared__ int64_t s_off[2][kMaxTile];
-  __shared__ __align__(16) float s_cs[2][TH];
-  __shared__ __align__(16) float s_sn[2][TH];
-  __shared__ int s_claim[2];
+  __shared__ int64_t s_off[kMaxTile];
+  __shared__ __align__(16) float s_cs[HALF > 0 ? HALF : 4];
+  __shared__ __align__(16) float s_sn[HALF > 0 ? HALF : 4];
+  __shared__ int s_next;  // the tile claimed for this CTA's next iteration
 
   const int g = threadIdx.x % G;
   const int u_first = threadIdx.x / G;
@@ -466,157 +339,167 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
   const int ka = g < NP ? g : g + NP;
   const int kb = g < NP ? g + NP : g + G;
   const int total = a.tiles_per_layer * a.n_layers;
-  const int tid = static_cast<int>(threadIdx.x);
 
-  // the first two tiles (each CTA stops claiming after its first index past
-  // the end, which keeps the claim count at tiles + grid)
-  int cur, nxt;
+  int w = blockIdx.x;
   if (a.dyn) {
-    if (tid == 0) {
-      const int c0 = claim_tile(a.err, total);
-      s_claim[0] = c0;
-      s_claim[1] = c0 < total ? claim_tile(a.err, total) : total;
-    }
+    if (threadIdx.x == 0) s_next = claim_tile(a.err, total);
     __syncthreads();
-    cur = s_claim[0];
-    nxt = s_claim[1];
-  } else {
-    cur = blockIdx.x;
-    nxt = cur + static_cast<int>(gridDim.x);
+    w = s_next;
   }
-  if (cur >= total) return;  // uniform across the CTA
+  // the next tile is claimed while this one is processed; s_next is written
+  // between the tile's two barriers and read after the second, and every
+  // thread has read it before the next iteration's first barrier
+  for (; w < total; w = a.dyn ? s_next : w + static_cast<int>(gridDim.x)) {
+    const int layer = w / a.tiles_per_layer;
+    const int tile = w - layer * a.tiles_per_layer;
 
-  // the first tile is resolved before the loop; every later one while its
-  // predecessor is moved
-  TileMove m;
-  {
-    const TilePlan p = plan_tile<HALF, SAVE>(a, cur);
-    if (tid == 0 && p.bits) atomicOr(a.err, p.bits);
-    if (p.m.ok) {
-      if (tid < p.m.nt) s_off[0][tid] = finish_slot(a, p, tid, fetch_slot(a, p, tid));
-      if (p.m.rot && tid < HALF) {
-        s_cs[0][tid] = p.tab[tid];
-        s_sn[0][tid] = p.tab[HALF + tid];
+    mshift_run run;
+    char* store;
+    int64_t cap;
+    char* kbase;
+    char* vbase;
+    const float* tab = nullptr;
+    bool ok_desc = true;
+    uint32_t bits = 0;
+    if (a.runs != nullptr) {
+      int lo = 0, hi = a.n_runs - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
       }
+      run = a.runs[lo];
+      const bool sess = run.session >= 0 && run.session < a.n_sessions;
+      store = sess ? static_cast<char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer])
+                   : nullptr;
+      cap = sess ? a.store_caps[run.session] : 0;
+      if (!sess || store == nullptr || !aligned16(store)) { ok_desc = false; bits |= MSHIFT_EBIT_SESSION; }
+      kbase = static_cast<char*>(a.k_ptrs[layer]);
+      vbase = static_cast<char*>(a.v_ptrs[layer]);
+      if (!SAVE) {
+        if (run.table >= 0 && run.table < a.n_tables) tab = a.tables + (int64_t)run.table * 2 * HALF;
+        else if (run.table != -1) { ok_desc = false; bits |= MSHIFT_EBIT_TABLE; }
+      }
+    } else {
+      run = a.run0;
+      store = static_cast<char*>(a.store0);
+      cap = a.cap0;
+      kbase = static_cast<char*>(a.k0);
+      vbase = static_cast<char*>(a.v0);
+      tab = SAVE ? nullptr : a.table0;
     }
-    m = p.m;
-  }
-  __syncthreads();
-
-  // units in the order of the side being written, so neighbouring threads
-  // store neighbouring rows: a load writes the paged cache, head-major when a
-  // head's tokens are adjacent there (HND); a save writes the token-major store
-  const bool head_major = !SAVE && a.head_stride > a.off_stride;
-  for (int i = 0; cur < total; ++i) {
-    const int b = i & 1;
-    const bool more = nxt < total;
-
-    // tile i + 1: descriptors now, block-table entries and table row in flight
-    TilePlan p;
-    TokenSlot ts{0, 0, false};
-    float pc = 0.f, ps = 0.f;
-    if (more) {
-      p = plan_tile<HALF, SAVE>(a, nxt);
-      if (tid == 0) {
-        if (p.bits) atomicOr(a.err, p.bits);
-        if (a.dyn) s_claim[b] = claim_tile(a.err, total);  // tile i + 2
-      }
-      if (p.m.ok) {
-        if (tid < p.m.nt) ts = fetch_slot(a, p, tid);
-        if (p.m.rot && tid < HALF) {
-          pc = p.tab[tid];
-          ps = p.tab[HALF + tid];
-        }
-      }
+    if (kbase == nullptr || vbase == nullptr || !aligned16(kbase) || !aligned16(vbase)) {
+      ok_desc = false;
+      bits |= MSHIFT_EBIT_SLOT;
     }
+    const int t0 = (tile - run.tile_begin) * a.tile_tokens;
+    const int nt = min(a.tile_tokens, run.len - t0);
+    const bool tile_ok = ok_desc && nt > 0 && t0 >= 0;
 
-    // tile i
-    if (m.ok) {
-      const bool rotate = m.rot && g < NP;
-      const int nt = m.nt;
-      const int nu = nt * a.heads;
-      const int64_t* off_s = s_off[b];
-      const float* cs_s = s_cs[b];
-      const float* sn_s = s_sn[b];
-      constexpr int U = MSHIFT_UNITS;
-      for (int u = u_first; u < nu; u += U * UPP) {
-        // U units per iteration: all 4*U loads are issued before any store
-        Vec k[U][2], v[U][2];
-        char* sp[U];
-        char* kp[U];
-        char* vp[U];
-        bool live[U];
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-          const int uu = u + q * UPP;
-          live[q] = false;
-          if (uu < nu) {
-            int t, h;
-            if (head_major) {
-              h = uu / nt;
-              t = uu - h * nt;
-            } else {
-              t = uu / a.heads;
-              h = uu - t * a.heads;
-            }
-            const int64_t off = off_s[t];
-            if (off >= 0) {
-              live[q] = true;
-              sp[q] = m.store + ((m.row0 + t) * a.st_tok + (int64_t)h * a.st_head) * ES;
-              kp[q] = m.kbase + (off + (int64_t)h * a.head_stride) * ES;
-              vp[q] = m.vbase + (off + (int64_t)h * a.head_stride) * ES;
-            }
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-          if (!live[q]) continue;
-          if (SAVE) {
-            k[q][0] = load_vec(kp[q] + ka * 16);
-            k[q][1] = load_vec(kp[q] + kb * 16);
-            v[q][0] = load_vec(vp[q] + g * 16);
-            v[q][1] = load_vec(vp[q] + (g + G) * 16);
-          } else {
-            k[q][0] = load_vec(sp[q] + ka * 16);
-            k[q][1] = load_vec(sp[q] + kb * 16);
-            v[q][0] = load_vec(sp[q] + D * ES + g * 16);
-            v[q][1] = load_vec(sp[q] + D * ES + (g + G) * 16);
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < U; ++q) {
-          if (!live[q]) continue;
-          if (rotate)
-            rotate_pair<E>(k[q][0], k[q][1], cs_s + g * VEC, sn_s + g * VEC);
-          if (SAVE) {
-            store_vec(sp[q] + ka * 16, k[q][0]);
-            store_vec(sp[q] + kb * 16, k[q][1]);
-            store_vec(sp[q] + D * ES + g * 16, v[q][0]);
-            store_vec(sp[q] + D * ES + (g + G) * 16, v[q][1]);
-          } else {
-            store_vec(kp[q] + ka * 16, k[q][0]);
-            store_vec(kp[q] + kb * 16, k[q][1]);
-            store_vec(vp[q] + g * 16, v[q][0]);
-            store_vec(vp[q] + (g + G) * 16, v[q][1]);
-          }
-        }
-      }
+    __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn / s_next
+    if (threadIdx.x == 0) {
+      if (bits) atomicOr(a.err, bits);
+      if (a.dyn) s_next = claim_tile(a.err, total);
     }
-
-    // tile i + 1's offsets and table row into the other buffer (last read by
-    // tile i - 1, before the previous barrier)
-    if (more && p.m.ok) {
-      if (tid < p.m.nt) s_off[b ^ 1][tid] = finish_slot(a, p, tid, ts);
-      if (p.m.rot && tid < HALF) {
-        s_cs[b ^ 1][tid] = pc;
-        s_sn[b ^ 1][tid] = ps;
+    if (tile_ok) {
+      for (int t = threadIdx.x; t < nt; t += kThreads) {
+        const int64_t spos = run.store_start + t0 + t;
+        int64_t slot;
+        bool slot_ok = true;
+        if (run.slots != nullptr) {
+          slot = run.slots[t0 + t];
+        } else {
+          const int64_t pos = run.paged_start + t0 + t;
+          const int64_t bi = pos >= 0 ? pos / a.block_size : -1;
+          slot_ok = bi >= 0 && bi < run.block_table_len;
+          slot = slot_ok ? (int64_t)run.block_table[bi] * a.block_size + pos % a.block_size : -1;
+        }
+        slot_ok = slot_ok && slot >= 0 && slot < a.num_slots;
+        const bool store_ok = spos >= 0 && spos < cap;
+        s_off[t] = (slot_ok && store_ok)
+                       ? (slot / a.block_size) * a.blk_stride + (slot % a.block_size) * a.off_stride
+                       : -1;
+        if (!slot_ok || !store_ok)
+          atomicOr(a.err, (slot_ok ? 0u : MSHIFT_EBIT_SLOT) | (store_ok ? 0u : MSHIFT_EBIT_STORE));
+      }
+      if (!SAVE && HALF > 0 && tab != nullptr) {
+        for (int i = threadIdx.x; i < HALF; i += kThreads) {
+          s_cs[i] = tab[i];
+          s_sn[i] = tab[HALF + i];
+        }
       }
     }
     __syncthreads();
-    cur = nxt;
-    if (more) {
-      m = p.m;
-      nxt = a.dyn ? s_claim[b] : nxt + static_cast<int>(gridDim.x);
+    if (!tile_ok) continue;
+
+    const bool rotate = !SAVE && HALF > 0 && tab != nullptr && g < NP;
+    const int nu = nt * a.heads;
+    // units in the order of the side being written, so neighbouring threads
+    // store neighbouring rows: a load writes the paged cache, head-major when a
+    // head's tokens are adjacent there (HND); a save writes the token-major store
+    const bool head_major = !SAVE && a.head_stride > a.off_stride;
+    const int64_t row0 = run.store_start + t0;
+    constexpr int U = MSHIFT_UNITS;
+    for (int u = u_first; u < nu; u += U * UPP) {
+      // U units per iteration: all 4*U loads are issued before any store
+      Vec k[U][2], v[U][2];
+      char* sp[U];
+      char* kp[U];
+      char* vp[U];
+      bool live[U];
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        const int uu = u + q * UPP;
+        live[q] = false;
+        if (uu < nu) {
+          int t, h;
+          if (head_major) {
+            h = uu / nt;
+            t = uu - h * nt;
+          } else {
+            t = uu / a.heads;
+            h = uu - t * a.heads;
+          }
+          const int64_t off = s_off[t];
+          if (off >= 0) {
+            live[q] = true;
+            sp[q] = store + ((row0 + t) * a.st_tok + (int64_t)h * a.st_head) * ES;
+            kp[q] = kbase + (off + (int64_t)h * a.head_stride) * ES;
+            vp[q] = vbase + (off + (int64_t)h * a.head_stride) * ES;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        if (!live[q]) continue;
+        if (SAVE) {
+          k[q][0] = load_vec(kp[q] + ka * 16);
+          k[q][1] = load_vec(kp[q] + kb * 16);
+          v[q][0] = load_vec(vp[q] + g * 16);
+          v[q][1] = load_vec(vp[q] + (g + G) * 16);
+        } else {
+          k[q][0] = load_vec(sp[q] + ka * 16);
+          k[q][1] = load_vec(sp[q] + kb * 16);
+          v[q][0] = load_vec(sp[q] + D * ES + g * 16);
+          v[q][1] = load_vec(sp[q] + D * ES + (g + G) * 16);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < U; ++q) {
+        if (!live[q]) continue;
+        if (rotate)
+          rotate_pair<E>(k[q][0], k[q][1], s_cs + g * VEC, s_sn + g * VEC);
+        if (SAVE) {
+          store_vec(sp[q] + ka * 16, k[q][0]);
+          store_vec(sp[q] + kb * 16, k[q][1]);
+          store_vec(sp[q] + D * ES + g * 16, v[q][0]);
+          store_vec(sp[q] + D * ES + (g + G) * 16, v[q][1]);
+        } else {
+          store_vec(kp[q] + ka * 16, k[q][0]);
+          store_vec(kp[q] + kb * 16, k[q][1]);
+          store_vec(vp[q] + g * 16, v[q][0]);
+          store_vec(vp[q] + (g + G) * 16, v[q][1]);
+        }
+      }
     }
   }
 }
