@@ -516,14 +516,18 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 // then release the stage through its "empty" mbarrier.  A caller tile of
 // `tile_tokens` tokens is split into parts that fit one stage.  Every copy is
 // a plain per-CTA copy from this GPU's own memory.
-// Stage ring per element type (measured best on B200, c2/c3 turns): three
-// stages of 32 KiB for e4m3, whose consumers are busier with arithmetic, and
-// of 24 KiB for 16/32-bit types; two CTAs per SM either way.
-// MSHIFT_BULK_STAGES / MSHIFT_BULK_STAGE_KB override both (tuning sweeps).
+// Per element type (measured best on B200, c2/c3 turns): three stages of
+// 24 KiB, two CTAs per SM; eight consumer warps for 16/32-bit types, four for
+// e4m3 (c3: 0.728 ms a turn against 0.750 with eight warps and 32 KiB stages,
+// 0.743 with four stages of 16 KiB).  MSHIFT_BULK_STAGES, MSHIFT_BULK_STAGE_KB,
+// MSHIFT_BULK_CONSUMER_WARPS and MSHIFT_BULK_MIN_BLOCKS override every type
+// (tuning sweeps).
 template <class E>
 struct BulkCfg {
   static constexpr int kStages = 3;
-  static constexpr int kStageBytes = (E::kScaled ? 32 : 24) * 1024;
+  static constexpr int kStageBytes = 24 * 1024;
+  static constexpr int kConsumerWarps = E::kScaled ? 4 : 8;
+  static constexpr int kMinBlocks = E::kScaled ? 3 : 2;
 };
 #ifdef MSHIFT_BULK_STAGES
 constexpr int kBulkStagesOverride = MSHIFT_BULK_STAGES;
@@ -637,25 +641,42 @@ struct BulkMeta {
   int rotate;  // the stage's table row is valid
 };
 
-#ifndef MSHIFT_BULK_CONSUMER_WARPS
-#define MSHIFT_BULK_CONSUMER_WARPS 8
-#endif
-#ifndef MSHIFT_BULK_MIN_BLOCKS
-#define MSHIFT_BULK_MIN_BLOCKS 2
-#endif
 #ifndef MSHIFT_BULK_UNITS_E4M3
 #define MSHIFT_BULK_UNITS_E4M3 1
 #endif
 constexpr int kBulkUnitsE4m3 = MSHIFT_BULK_UNITS_E4M3;
-constexpr int kBulkConsumerWarps = MSHIFT_BULK_CONSUMER_WARPS;  // warps that rotate and store
-constexpr int kBulkConsumers = kBulkConsumerWarps * 32;
-constexpr int kBulkThreads = kBulkConsumers + 32;              // + one producer warp
+#ifdef MSHIFT_BULK_CONSUMER_WARPS
+constexpr int kBulkWarpsOverride = MSHIFT_BULK_CONSUMER_WARPS;
+#else
+constexpr int kBulkWarpsOverride = 0;
+#endif
+#ifdef MSHIFT_BULK_MIN_BLOCKS
+constexpr int kBulkMinBlocksOverride = MSHIFT_BULK_MIN_BLOCKS;
+#else
+constexpr int kBulkMinBlocksOverride = 0;
+#endif
+// warps that rotate and store, the CTA (those + one producer warp), and the
+// resident CTAs per SM the register allocation is sized for
+template <class E>
+__host__ __device__ constexpr int bulk_consumer_warps() {
+  return kBulkWarpsOverride ? kBulkWarpsOverride : BulkCfg<E>::kConsumerWarps;
+}
+template <class E>
+__host__ __device__ constexpr int bulk_threads() {
+  return bulk_consumer_warps<E>() * 32 + 32;
+}
+template <class E>
+__host__ __device__ constexpr int bulk_min_blocks() {
+  return kBulkMinBlocksOverride ? kBulkMinBlocksOverride : BulkCfg<E>::kMinBlocks;
+}
 
 template <class E, int D, int ROT>
-__global__ void __launch_bounds__(kBulkThreads, MSHIFT_BULK_MIN_BLOCKS) bulk_load_kernel(
-    const KArgs a, int parts,
-                                                                     int part_tokens) {
+__global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_load_kernel(
+    const KArgs a, int parts, int part_tokens) {
   wait_prior_grid();
+  constexpr int kBulkConsumerWarps = bulk_consumer_warps<E>();
+  constexpr int kBulkConsumers = kBulkConsumerWarps * 32;
+  constexpr int kBulkThreads = bulk_threads<E>();
   constexpr int ES = E::kBytes;
   constexpr int VEC = E::kVec;
   constexpr int NV = D / VEC;
@@ -935,12 +956,12 @@ struct Variant {
   KernelFn load;
   KernelFn save;
   BulkFn bulk;
-  int bulk_stages, bulk_stage_bytes;
+  int bulk_stages, bulk_stage_bytes, bulk_threads;
 };
 
 #define MSHIFT_VARIANT(E, DT, D, R)                                                    \
   {DT, D, R, move_kernel<E, D, R, false>, move_kernel<E, D, D, true>,                 \
-   bulk_load_kernel<E, D, R>, bulk_stages<E>(), bulk_stage_bytes<E>()}
+   bulk_load_kernel<E, D, R>, bulk_stages<E>(), bulk_stage_bytes<E>(), bulk_threads<E>()}
 
 const Variant kVariants[] = {
     MSHIFT_VARIANT(Bf16, MSHIFT_BF16, 128, 128),
@@ -1110,7 +1131,7 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
       e = cudaFuncSetAttribute(v->bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       int occ = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v->bulk, kBulkThreads, smem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, v->bulk, v->bulk_threads, smem);
       if (e != cudaSuccess) return cuda_fail(e);
       if (occ < 1) return MSHIFT_EUNSUPPORTED;
       g_grid.bulk_smem[dev][vi] = smem;
@@ -1120,9 +1141,10 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
     grid = static_cast<int>(items < cap ? items : cap);
   }
   if (pdl) {
-    e = launch_dependent(v->bulk, dim3(grid), dim3(kBulkThreads), smem, stream, args, parts, part);
+    e = launch_dependent(v->bulk, dim3(grid), dim3(v->bulk_threads), smem, stream, args, parts,
+                         part);
   } else {
-    v->bulk<<<grid, kBulkThreads, smem, stream>>>(args, parts, part);
+    v->bulk<<<grid, v->bulk_threads, smem, stream>>>(args, parts, part);
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);
