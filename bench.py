@@ -529,12 +529,15 @@ def load_step(launcher, wl, ev=None, check=False) -> tuple[int, int]:
 def timed_turns(step, steps: int, ranks: Ranks, detail: dict | None = None):
     """``steps`` turns back to back, CUDA events around all of them (barrier and
     sync on both sides), max over ranks; kernel durations sampled on every
-    ``steps // 25``-th turn (an event pair costs a turn a few microseconds, which
-    sampling every turn would charge to the whole-job number).
+    ``max(4, steps // 25)``-th turn.  An event pair between two turns costs a
+    turn a few microseconds -- it separates the previous turn's load kernel
+    from this turn's table kernel, which otherwise launch as programmatic
+    dependents and overlap -- so sampling every turn would charge that to the
+    whole-job number.
     Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms,
     launches); with ``detail``, also every rank's device ms per turn, mean
     sampled kernel ms and host (issuing) ms per turn."""
-    stride = max(1, steps // 25)
+    stride = max(4, steps // 25)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(0, steps, stride)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
