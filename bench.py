@@ -717,9 +717,10 @@ def c4_extra(args, ranks: Ranks) -> dict:
 
     cfg = config("c4")
     lo, hi = head_shard(cfg.heads, ranks.rank, ranks.world)
+    # store rows of every session plus a paged cache of about the same size
     need = sum(cfg.history) * cfg.layers * cfg.bytes_per_token_layer(hi - lo)
     free, _ = torch.cuda.mem_get_info(ranks.device)
-    if ranks.max(float(need > 0.9 * free)) > 0:  # one decision for every rank
+    if ranks.max(float(need + (4 << 30) > free)) > 0:  # one decision for every rank
         return {"config": workload_config(cfg, ranks.world, args.layout),
                 "skipped": f"needs about {need / 1e9:.0f} GB per GPU at {hi - lo} heads"}
     wl = build(cfg, ranks.device, head_lo=lo, head_hi=hi, layout=args.layout)
