@@ -307,45 +307,6 @@ __device__ __forceinline__ int claim_tile(uint32_t* err, int total) {
   return t;
 }
 
-#ifndef MSHIFT_PREFETCH_NEXT
-#define MSHIFT_PREFETCH_NEXT 0
-#endif
-
-// L2 prefetch of tile w's store rows: rows [row0, row0 + nt) of the run's
-// session buffer for the tile's layer, clipped to the buffer's capacity -- one
-// contiguous, 16-byte aligned range (row stride st_tok * ES is a multiple of
-// 16 bytes, checked on the host), requested with one bulk prefetch.  Only
-// dense rows (every byte of the range belongs to the buffer) and valid
-// descriptors are prefetched; anything else is skipped.
-template <int ES, int D>
-__device__ __forceinline__ void prefetch_tile_rows(const KArgs& a, int w) {
-  if (a.runs == nullptr || a.st_head != 2 * D || a.st_tok != (int64_t)a.heads * 2 * D) return;
-  const int layer = w / a.tiles_per_layer;
-  const int tile = w - layer * a.tiles_per_layer;
-  int lo = 0, hi = a.n_runs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (a.runs[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
-  }
-  const mshift_run& run = a.runs[lo];
-  if (run.session < 0 || run.session >= a.n_sessions) return;
-  const char* store =
-      static_cast<const char*>(a.store_ptrs[(int64_t)run.session * a.n_layers + layer]);
-  if (store == nullptr || !aligned16(store)) return;
-  const int64_t t0 = (int64_t)(tile - run.tile_begin) * a.tile_tokens;
-  const int64_t first = run.store_start + t0;
-  int64_t last = first + min((int64_t)a.tile_tokens, (int64_t)run.len - t0);
-  const int64_t cap = a.store_caps[run.session];
-  if (last > cap) last = cap;
-  if (t0 < 0 || first < 0 || last <= first) return;
-  const int64_t row_bytes = a.st_tok * ES;
-  const int64_t bytes = (last - first) * row_bytes;
-  if (bytes <= 0 || bytes > (int64_t{1} << 30) || (row_bytes & 15)) return;
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(store + first * row_bytes),
-               "r"(static_cast<uint32_t>(bytes))
-               : "memory");
-}
-
 // One templated kernel for both directions.
 //   SAVE = false: store rows -> paged cache, K rotated (load)
 //   SAVE = true : paged cache -> store rows, bit copy (save)
@@ -437,13 +398,7 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
     __syncthreads();  // the previous tile is done with s_off / s_cs / s_sn / s_next
     if (threadIdx.x == 0) {
       if (bits) atomicOr(a.err, bits);
-      const int next = a.dyn ? claim_tile(a.err, total) : w + static_cast<int>(gridDim.x);
-      if (a.dyn) s_next = next;
-#if MSHIFT_PREFETCH_NEXT
-      // loads: ask L2 for the next tile's store rows (one contiguous range)
-      // while this tile moves, so its loads find them there
-      if (!SAVE && next < total) prefetch_tile_rows<ES, D>(a, next);
-#endif
+      if (a.dyn) s_next = claim_tile(a.err, total);
     }
     if (tile_ok) {
       for (int t = threadIdx.x; t < nt; t += kThreads) {
