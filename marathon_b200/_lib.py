@@ -173,6 +173,9 @@ def check(status: int, what: str) -> None:
 
 
 def describe_bits(bits: int) -> str:
+    """Names of the ``MSHIFT_EBIT_*`` flags in a status word (its low 8 bits;
+    bits 8..31 are the tile-claim count a batched launch uses while it runs)."""
+    bits &= 0xFF
     names = []
     for bit, name in (
         (EBIT_SLOT, "slot outside the paged cache"),
