@@ -67,7 +67,7 @@
 namespace mshift {
 
 constexpr int kThreads = 256;  // threads per CTA
-constexpr int kMaxTile = 256;  // tokens per tile, upper bound (smem sizing)
+constexpr int kMaxTile = 512;  // tokens per tile, upper bound (smem sizing)
 constexpr int kMaxDevices = 64;
 
 struct alignas(16) Vec {
@@ -514,8 +514,10 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
 // run's cos/sin row) and its lane 0 issues the bulk copy; eight consumer
 // warps rotate K from shared memory and write K and V with 128-bit stores,
 // then release the stage through its "empty" mbarrier.  A caller tile of
-// `tile_tokens` tokens is split into parts that fit one stage.  Every copy is
-// a plain per-CTA copy from this GPU's own memory.
+// `tile_tokens` tokens is split into parts that fit one stage; the producer
+// claims whole tiles as move_kernel does (dynamic, one claim per tile) and
+// publishes their parts in order, then an end-of-work stage that sends the
+// consumers out.  Every copy is a plain per-CTA copy from this GPU's own memory.
 // Per element type (measured best on B200, c2/c3 turns): three stages of
 // 24 KiB, two CTAs per SM; eight consumer warps for 16/32-bit types, four for
 // e4m3 (c3: 0.728 ms a turn against 0.750 with eight warps and 32 KiB stages,
@@ -674,6 +676,7 @@ template <class E, int D, int ROT>
 __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_load_kernel(
     const KArgs a, int parts, int part_tokens) {
   wait_prior_grid();
+  allow_dependents();  // as in move_kernel: the next turn's table kernel may launch
   constexpr int kBulkConsumerWarps = bulk_consumer_warps<E>();
   constexpr int kBulkConsumers = kBulkConsumerWarps * 32;
   constexpr int kBulkThreads = bulk_threads<E>();
@@ -700,7 +703,6 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
   const int warp = threadIdx.x >> 5;
   const int64_t row_bytes = (int64_t)a.heads * 2 * D * ES;
   const int64_t stage_bytes = (int64_t)part_tokens * row_bytes;
-  const int total = a.tiles_per_layer * a.n_layers * parts;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -726,9 +728,41 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
     const float* tab = nullptr;
     uint32_t desc_bits = 0;
     bool desc_ok = false;
-    int k = 0;
-    for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
+    int k = 0;  // stages published so far (the end-of-work stage included)
+    // The producer takes whole tiles -- claimed (dynamic) or this CTA's stride
+    // of tiles (static) -- and publishes their parts in order, so a launch
+    // makes one claim per tile, not per stage.  A claim runs one tile ahead:
+    // lane 0 issues the next claim as soon as it has read the current one, so
+    // the atomic's round trip overlaps the tile's stages.  Same protocol as
+    // claim_tile: claims stop at the first index >= tiles, and whoever draws
+    // tiles + gridDim.x - 1 clears the counter bits.
+    const int tiles = a.tiles_per_layer * a.n_layers;
+    int w = 0;         // the current tile
+    int part = parts;  // its next part (parts: take a new tile)
+    int taken = 0;     // static: tiles this CTA has taken
+    bool done = false;
+    uint32_t ahead = 0;
+    if (a.dyn && lane == 0) ahead = atomicAdd(a.err, 256u);
+    for (;; ++k) {
       const int s = k % NS;
+      if (part == parts) {
+        int64_t next;
+        if (a.dyn) {
+          int c = 0;
+          if (lane == 0) {
+            c = static_cast<int>(ahead >> 8);
+            if (c == tiles + static_cast<int>(gridDim.x) - 1) atomicAnd(a.err, 0xFFu);
+            if (c < tiles) ahead = atomicAdd(a.err, 256u);
+          }
+          next = __shfl_sync(0xffffffffu, c, 0);
+        } else {
+          next = (int64_t)blockIdx.x + (int64_t)taken * gridDim.x;
+          ++taken;
+        }
+        done = next >= tiles;
+        w = done ? 0 : static_cast<int>(next);
+        part = 0;
+      }
       if (warp_saw_abort(&s_abort)) break;  // a consumer warp gave up: issue nothing more
       if (k >= NS) {
         if (!warp_mbar_wait(&s_empty[s], ((k / NS) - 1) & 1, kWaitLimit, &s_abort)) {
@@ -737,8 +771,16 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
           break;
         }
       }
-      const int w = item / parts;
-      const int part = item - w * parts;
+      if (done) {
+        // no more tiles: an end-of-work stage (nt = -1) sends the consumers out
+        if (lane == 0) {
+          s_meta[s].nt = -1;
+          mbar_arrive(&s_full[s]);
+        }
+        ++k;
+        break;
+      }
+      const int this_part = part++;
       const int layer = w / a.tiles_per_layer;
       const int tile = w - layer * a.tiles_per_layer;
       const bool same_run = cur_run >= 0 && tile >= run.tile_begin && tile < next_begin;
@@ -778,8 +820,8 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
       uint32_t bits = desc_bits;
       const bool ok = desc_ok;
       const int t_tile = (tile - run.tile_begin) * a.tile_tokens;
-      const int t0 = t_tile + part * part_tokens;
-      const int nt = min(min(part_tokens, a.tile_tokens - part * part_tokens), run.len - t0);
+      const int t0 = t_tile + this_part * part_tokens;
+      const int nt = min(min(part_tokens, a.tile_tokens - this_part * part_tokens), run.len - t0);
       const int64_t row0 = run.store_start + t0;
       int nvalid = 0;
       if (ok && nt > 0 && t_tile >= 0 && row0 >= 0) {
@@ -855,8 +897,7 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
   const int u_first = threadIdx.x / G;
   const int ka = g < NP ? g : g + NP;
   const int kb = g < NP ? g + NP : g + G;
-  int k = 0;
-  for (int item = blockIdx.x; item < total; item += gridDim.x, ++k) {
+  for (int k = 0;; ++k) {
     const int s = k % NS;
     const uint32_t limit = (k == 0 && a.first_wait != 0u) ? a.first_wait - 1u : kWaitLimit;
     if (!warp_mbar_wait(&s_full[s], (k / NS) & 1, limit, &s_abort)) {
@@ -865,6 +906,7 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
       break;
     }
     const BulkMeta m = s_meta[s];
+    if (m.nt < 0) break;  // the producer's end-of-work stage
     const unsigned char* stage = s_data + s * stage_bytes;
     const int nu = m.nt * a.heads;
     const bool rotate = m.rotate && g < NP;
@@ -1110,8 +1152,8 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
   if (part > kBulkMaxPart) part = kBulkMaxPart;
   if (part < 1) return MSHIFT_EUNSUPPORTED;
   const int parts = (args.tile_tokens + part - 1) / part;
-  const int64_t items = (int64_t)args.tiles_per_layer * args.n_layers * parts;
-  if (items > INT32_MAX) return MSHIFT_EUNSUPPORTED;
+  const int64_t tiles = (int64_t)args.tiles_per_layer * args.n_layers;
+  if (tiles * parts > INT32_MAX) return MSHIFT_EUNSUPPORTED;
   const int smem = static_cast<int>(v->bulk_stages * part * row_bytes);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1137,14 +1179,19 @@ int launch_bulk(const Variant* v, const KArgs& args, int64_t row_bytes, cudaStre
       g_grid.bulk_smem[dev][vi] = smem;
       g_grid.bulk_occ[dev][vi] = occ;
     }
+    // a CTA works through whole tiles, so more CTAs than tiles would idle
     const int64_t cap = (int64_t)g_grid.sms[dev] * g_grid.bulk_occ[dev][vi];
-    grid = static_cast<int>(items < cap ? items : cap);
+    grid = static_cast<int>(tiles < cap ? tiles : cap);
   }
+  // tiles are claimed dynamically while the claim counter fits bits 8..31 of
+  // the status word, as in the 128-bit-load kernel
+  KArgs a = args;
+  a.dyn = (a.runs != nullptr && tiles + grid < (int64_t{1} << 24)) ? 1 : 0;
   if (pdl) {
-    e = launch_dependent(v->bulk, dim3(grid), dim3(v->bulk_threads), smem, stream, args, parts,
+    e = launch_dependent(v->bulk, dim3(grid), dim3(v->bulk_threads), smem, stream, a, parts,
                          part);
   } else {
-    v->bulk<<<grid, v->bulk_threads, smem, stream>>>(args, parts, part);
+    v->bulk<<<grid, v->bulk_threads, smem, stream>>>(a, parts, part);
     e = cudaGetLastError();
   }
   return e == cudaSuccess ? MSHIFT_OK : cuda_fail(e);

@@ -444,7 +444,6 @@ class Launcher:
         self.staging = _Staging(self.device, self.lib, staging_slots)
         self._copy_stream = None
         self._upload_events = [torch.cuda.Event() for _ in range(staging_slots)]
-        self._tiles: dict = {}
         self.last_launches = 0
         self.last_h2d = 0  # bytes of the last batch's descriptor copy
         self._tables: list[torch.Tensor | None] = [None] * staging_slots
@@ -490,37 +489,39 @@ class Launcher:
         """
         self.staging.drain()
 
-    #: per-tile cost in (token, head) units: barriers, slot resolution, table staging
-    TILE_OVERHEAD_UNITS = 16
+    #: (token, head) units per tile of a batched launch.  Both load kernels and
+    #: the save kernel claim tiles dynamically, so a launch ends within one tile
+    #: of its fastest CTA whatever the tile count; the tile only has to amortise
+    #: its fixed cost (the claim, two barriers, slot resolution, table staging)
+    #: and fill whole passes of 64 units.  Measured on B200 (c2 turn at 1/2/4/8
+    #: heads per rank, tiles of 128-1024 units): 256 units is best or within
+    #: noise of it up to about 64 tiles per resident CTA; beyond that (a full
+    #: 8-head c2 turn has 121) 448 units is 0.7% faster.  An e4m3 cache is
+    #: served by the TMA kernel, which splits a tile into 24 KiB stages: 384
+    #: units (256 bytes each) are four full stages at any head count, and a
+    #: ragged last stage costs about 3% (c3 turn, tiles of 192-1152 units).
+    TILE_UNITS = 256
+    TILE_UNITS_LARGE = 448
+    TILE_UNITS_E4M3 = 384
+    LARGE_TILES_PER_CTA = 64
+    #: bounds of tokens per tile (the kernels accept 1..512)
+    TILE_TOKENS_MIN, TILE_TOKENS_MAX = 16, 512
 
     def _tile_for(self, tokens: int, n_layers: int, lengths=None) -> int:
-        """Tokens per tile that balance the launch's last wave.
+        """Tokens per tile for a batch of ``tokens`` tokens over ``n_layers`` layers.
 
-        Tiles of 256 (token, head) units are the measured best; smaller tiles
-        pay per-tile overhead.  Between 128 and 256 units, pick the size that
-        minimises the most any CTA does: (tiles per CTA, rounded up) x (tile
-        units + per-tile overhead).  A short launch (one head per rank) gets a
-        tile count just under a multiple of the resident CTAs instead of a
-        last wave that leaves most of them idle.
+        ``TILE_UNITS`` units per tile, or ``TILE_UNITS_LARGE`` for launches with
+        more than ``LARGE_TILES_PER_CTA`` tiles of ``TILE_UNITS`` per resident
+        CTA, or ``TILE_UNITS_E4M3`` for an e4m3 cache, divided by this rank's
+        heads.
         """
-        key = (n_layers, tokens if lengths is None else tuple(lengths))
-        hit = self._tiles.get(key)
-        if hit is not None:
-            return hit
-        if len(self._tiles) > 4096:
-            self._tiles.clear()
-        self._tiles[key] = tt = self._tile_search(tokens, n_layers, lengths)
-        return tt
-
-    def _tile_search(self, tokens: int, n_layers: int, lengths) -> int:
         heads = self.geo.heads
-        t_max = max(1, int(self.lib.mshift_default_tile_tokens(heads)))
-        t_min = max(1, t_max // 2)
-        lens = np.asarray([tokens] if lengths is None else lengths, dtype=np.int64)
-        cand = np.arange(t_max, t_min - 1, -1, dtype=np.int64)
-        tiles = n_layers * (-(-lens[:, None] // cand[None, :])).sum(axis=0)
-        cost = -(-tiles // self._grid) * (cand * heads + self.TILE_OVERHEAD_UNITS)
-        return int(cand[int(np.argmin(cost))])  # first minimum: the largest tile
+        units = self.TILE_UNITS
+        if self.geo.dtype == _lib.E4M3:
+            units = self.TILE_UNITS_E4M3
+        elif tokens * n_layers * heads > self.LARGE_TILES_PER_CTA * self._grid * self.TILE_UNITS:
+            units = self.TILE_UNITS_LARGE
+        return int(min(max(units // heads, self.TILE_TOKENS_MIN), self.TILE_TOKENS_MAX))
 
     # -- packing ------------------------------------------------------------
     _RUN = struct.Struct("<qqQQiiiiii")  # mshift_run, 56 bytes

@@ -54,14 +54,13 @@ class _FakeSlots:
         return self.addr
 
 
-def _launcher(heads: int, small: int) -> Launcher:
+def _launcher(heads: int, small: int, dtype: int = _lib.BF16) -> Launcher:
     la = object.__new__(Launcher)
-    la.geo = SimpleNamespace(heads=heads)
+    la.geo = SimpleNamespace(heads=heads, dtype=dtype)
     la.lib = _lib.load()
     la.fixed_tile = False
     la.tile_tokens = int(la.lib.mshift_default_tile_tokens(heads))
     la._grid = 296
-    la._tiles = {}
     la.staging = _FakeStaging()
     la.last_h2d = 0
     la._SMALL = small
@@ -137,3 +136,25 @@ def test_packed_records_describe_the_runs(seed):
     if deltas:
         d = host[p.deltas - BASE : p.deltas - BASE + 8 * len(deltas)].view(np.int64)
         assert d.tolist() == deltas
+
+
+@pytest.mark.parametrize("heads,tokens,layers,want", [
+    (8, 28_608, 40, 56),    # full c2 turn: 121 tiles of 256 units per CTA -> 448 units
+    (4, 28_608, 40, 64),    # a TP2 rank's share: 60 per CTA -> 256 units
+    (2, 28_608, 40, 128),
+    (1, 28_608, 40, 256),   # a TP8 rank's share
+    (1, 600_000, 40, 448),  # one head, but a long batch
+    (64, 1_000, 4, 16),     # many heads: the 16-token floor
+    (8, 10, 1, 32),         # a tiny batch
+])
+def test_tile_rule(heads, tokens, layers, want):
+    la = _launcher(heads, small=32)
+    assert la._tile_for(tokens, layers) == want
+
+
+@pytest.mark.parametrize("heads,want", [(8, 48), (4, 96), (2, 192), (1, 384)])
+def test_tile_rule_e4m3_is_whole_tma_stages(heads, want):
+    """384 units of 256 bytes: four 24 KiB stages of the TMA kernel at any head count."""
+    la = _launcher(heads, small=32, dtype=_lib.E4M3)
+    assert la._tile_for(28_608, 40) == want
+    assert want * heads * 256 == 4 * 24 * 1024
