@@ -19,7 +19,9 @@
  *     count the tiles its CTAs have claimed (they are cleared again before the
  *     launch completes), so one status word must not be shared by launches
  *     that can run at the same time; launches ordered on one stream may share
- *     it and accumulate their flags.
+ *     it and accumulate their flags.  A CTA's claims strictly increase within
+ *     a launch; a CTA that draws one that does not (the counter was reset by
+ *     another launch on the same word) sets MSHIFT_EBIT_CLAIM and stops.
  *
  * Layout vocabulary (shared with the Python package marathon_b200):
  *   store    one buffer per (session, layer): [capacity, heads, 2*head_size],
@@ -66,6 +68,8 @@ extern "C" {
 #define MSHIFT_EBIT_SESSION 4u /* run.session outside [0, n_sessions) or null buffer */
 #define MSHIFT_EBIT_TABLE 8u   /* run.table outside [-1, n_tables)           */
 #define MSHIFT_EBIT_TIMEOUT 16u /* a bulk copy did not complete in time; the launch stopped */
+#define MSHIFT_EBIT_CLAIM 32u   /* the tile-claim counter went backwards (the status word
+                                   was shared with a launch in flight); the launch stopped */
 
 /* ---- element types ----------------------------------------------------- */
 #define MSHIFT_BF16 0

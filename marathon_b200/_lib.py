@@ -18,7 +18,7 @@ import numpy as np
 LIB_PATH = Path(__file__).resolve().parent / "libmarathon_shift.so"
 
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETOOBIG = 0, 1, 2, 3, 4
-EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE, EBIT_TIMEOUT = 1, 2, 4, 8, 16
+EBIT_SLOT, EBIT_STORE, EBIT_SESSION, EBIT_TABLE, EBIT_TIMEOUT, EBIT_CLAIM = 1, 2, 4, 8, 16, 32
 BF16, F16, F32, E4M3 = 0, 1, 2, 3
 KERNEL_LSU, KERNEL_BULK, KERNEL_AUTO = 0, 1, 2
 
@@ -183,6 +183,8 @@ def describe_bits(bits: int) -> str:
         (EBIT_SESSION, "bad session index or missing store buffer"),
         (EBIT_TABLE, "bad rotation-table index"),
         (EBIT_TIMEOUT, "a bulk copy did not complete in time; the launch stopped early"),
+        (EBIT_CLAIM, "the tile-claim counter went backwards (status word shared with a "
+                     "launch in flight); the launch stopped early"),
     ):
         if bits & bit:
             names.append(name)

@@ -349,7 +349,16 @@ __global__ void __launch_bounds__(kThreads, MSHIFT_MIN_BLOCKS) move_kernel(const
   // the next tile is claimed while this one is processed; s_next is written
   // between the tile's two barriers and read after the second, and every
   // thread has read it before the next iteration's first barrier
+  int prev = -1;
   for (; w < total; w = a.dyn ? s_next : w + static_cast<int>(gridDim.x)) {
+    // a CTA's claims strictly increase within a launch; one that does not
+    // means the counter was reset under it (a status word shared with another
+    // launch in flight): stop with an error instead of taking tiles again
+    if (w <= prev) {
+      if (threadIdx.x == 0) atomicOr(a.err, MSHIFT_EBIT_CLAIM);
+      break;
+    }
+    prev = w;
     const int layer = w / a.tiles_per_layer;
     const int tile = w - layer * a.tiles_per_layer;
 
@@ -739,7 +748,7 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
     const int tiles = a.tiles_per_layer * a.n_layers;
     int w = 0;         // the current tile
     int part = parts;  // its next part (parts: take a new tile)
-    int taken = 0;     // static: tiles this CTA has taken
+    int taken = 0;     // tiles this CTA has taken
     bool done = false;
     uint32_t ahead = 0;
     if (a.dyn && lane == 0) ahead = atomicAdd(a.err, 256u);
@@ -755,6 +764,12 @@ __global__ void __launch_bounds__(bulk_threads<E>(), bulk_min_blocks<E>()) bulk_
             if (c < tiles) ahead = atomicAdd(a.err, 256u);
           }
           next = __shfl_sync(0xffffffffu, c, 0);
+          // claims strictly increase within a launch (see move_kernel)
+          if (next <= w && taken > 0) {
+            if (lane == 0) atomicOr(a.err, MSHIFT_EBIT_CLAIM);
+            next = tiles;
+          }
+          ++taken;
         } else {
           next = (int64_t)blockIdx.x + (int64_t)taken * gridDim.x;
           ++taken;

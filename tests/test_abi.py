@@ -134,3 +134,14 @@ def test_stage_validates_before_touching_cuda(lib):
     assert lib.mshift_stage(rec.ctypes.data, 2, None) == _lib.EINVAL
     rec[1] = (0, 4096, 16)  # bytes with a null destination
     assert lib.mshift_stage(rec.ctypes.data, 2, None) == _lib.EINVAL
+
+
+def test_status_flags_match_the_header():
+    """Every MSHIFT_EBIT_* flag of the header has the same value in the binding."""
+    text = (Path(__file__).resolve().parents[1] / "include" / "marathon_shift.h").read_text()
+    flags = {m[1]: int(m[2]) for m in re.finditer(r"#define MSHIFT_EBIT_(\w+) (\d+)u", text)}
+    assert flags == {"SLOT": 1, "STORE": 2, "SESSION": 4, "TABLE": 8, "TIMEOUT": 16, "CLAIM": 32}
+    for name, value in flags.items():
+        assert getattr(_lib, f"EBIT_{name}") == value
+        assert _lib.describe_bits(value) != "none"
+    assert max(flags.values()) < 256  # the low 8 bits; bits 8..31 carry the claim count
