@@ -528,16 +528,17 @@ def load_step(launcher, wl, ev=None, check=False) -> tuple[int, int]:
 
 def timed_turns(step, steps: int, ranks: Ranks, detail: dict | None = None):
     """``steps`` turns back to back, CUDA events around all of them (barrier and
-    sync on both sides), max over ranks; kernel durations sampled on every
-    ``max(4, steps // 25)``-th turn.  An event pair between two turns costs a
-    turn a few microseconds -- it separates the previous turn's load kernel
+    sync on both sides), max over ranks; kernel durations sampled on about
+    three turns spread over the region (every ``max(8, ceil(steps / 3))``-th).
+    An event pair between two turns separates the previous turn's load kernel
     from this turn's table kernel, which otherwise launch as programmatic
-    dependents and overlap -- so sampling every turn would charge that to the
-    whole-job number.
+    dependents and overlap: measured on B200, sampling every fourth turn
+    added 2.8 us to a one-head turn (1.5%) and every turn 8 us, so the
+    samples are kept few to leave the whole-job number undisturbed.
     Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms,
     launches); with ``detail``, also every rank's device ms per turn, mean
     sampled kernel ms and host (issuing) ms per turn."""
-    stride = max(4, steps // 25)
+    stride = max(8, -(-steps // 3))
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(0, steps, stride)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -335,6 +335,7 @@ class _Staging:
         self.used = [False] * self.n
         self.slot = 0
         self.err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._status_stream = None  # status-word read-backs off the launch stream
         # per slot: [upload record, error-word read-back record]
         self.rec = np.zeros((self.n, 2), dtype=_lib.COPY_DTYPE)
         self.rec_addr = self.rec.ctypes.data
@@ -383,6 +384,28 @@ class _Staging:
         """Queue a copy of the slot's error word into ``dst`` (pinned int32 [1]) on ``stream``."""
         with torch.cuda.stream(stream):
             dst.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
+
+    def copy_err_after(self, slot: int, dst: torch.Tensor, after) -> torch.cuda.Event:
+        """Copy the slot's error word into ``dst`` (pinned int32 [1]) once the event
+        ``after`` (recorded behind the batch's kernels) has completed, on a side
+        stream of the ring's own; returns the event that marks the copy done.
+
+        Nothing is queued on the launch stream: a copy there would sit between
+        this batch's load kernel and the next batch's table kernel, which then
+        could no longer launch while the load finishes (programmatic dependent
+        launch).  The slot stays busy until the copy has read the word, so the
+        next batch's descriptor upload cannot zero it first.
+        """
+        if self._status_stream is None:
+            self._status_stream = torch.cuda.Stream(self.device)
+        st = self._status_stream
+        st.wait_event(after)
+        with torch.cuda.stream(st):
+            dst.copy_(self.dev[slot][:4].view(torch.int32), non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(st)
+        self.finish(slot, st)
+        return done
 
     def read_err(self, slot: int, stream) -> int:
         rec = self.rec_addr + (slot * 2 + 1) * _lib.COPY_DTYPE.itemsize

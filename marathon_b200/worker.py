@@ -202,16 +202,16 @@ class ShiftWorker:
 
     def _queue_load(self, runs, view) -> StagedLoad:
         """One launch on the current stream; its status word is copied back
-        asynchronously and read in ``finish_pending``."""
+        asynchronously, off that stream, and read in ``finish_pending``."""
         la = self.launcher
         p = la.prepare_load(runs, view, self.inv, k_scales=self.k_scales)
         la.launch(p)
-        errs = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-        la.staging.copy_err(p.slot, errs, p.stream)
         la.finish(p, False)
         done = torch.cuda.Event()
         done.record(p.stream)
-        return StagedLoad([done] * len(self.layers), done, errs, 1, same_stream=True)
+        errs = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        copied = la.staging.copy_err_after(p.slot, errs, done)
+        return StagedLoad([done] * len(self.layers), copied, errs, 1, same_stream=True)
 
     def wait_layer(self, name: str) -> None:
         """Order the current stream after layer ``name`` of a pending staged load."""
