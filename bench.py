@@ -19,7 +19,10 @@ whole turn's algorithmic bytes over the max-over-ranks device time.
 
 Printed JSON keys beyond the driver's base contract:
   roofline      load kernel: algorithmic bytes per launch / mean CUDA-event
-                duration of that launch, against the measured HBM copy peak
+                duration of that launch (the first and last turns of the
+                timed region), against the measured HBM copy peak;
+                isolated_turns: best and median of 10 single event-timed turns
+                after the timed region
   e2e           the same turn through the public worker API (ShiftWorker.load)
                 from host metadata: block table + descriptors copied from pinned
                 host memory, tables + load kernels, the 4-byte status read back;
@@ -526,42 +529,70 @@ def load_step(launcher, wl, ev=None, check=False) -> tuple[int, int]:
     return n, p.h2d_bytes
 
 
+#: GPU cycles of the sleep queued ahead of a timed region (about 0.3 ms):
+#: the stream stays busy while the host packs the region's first turn
+LEAD_CYCLES = 600_000
+
+
 def timed_turns(step, steps: int, ranks: Ranks, detail: dict | None = None):
     """``steps`` turns back to back, CUDA events around all of them (barrier and
-    sync on both sides), max over ranks; kernel durations sampled on about
-    three turns spread over the region (every ``max(8, ceil(steps / 3))``-th).
-    An event pair between two turns separates the previous turn's load kernel
-    from this turn's table kernel, which otherwise launch as programmatic
-    dependents and overlap: measured on B200, sampling every fourth turn
-    added 2.8 us to a one-head turn (1.5%) and every turn 8 us, so the
-    samples are kept few to leave the whole-job number undisturbed.
+    sync on both sides), max over ranks.
+
+    Kernel durations are sampled on the first and the last turn.  Their outer
+    events coincide with the region's own, so only two turn boundaries lose
+    the overlap of a load kernel with the next turn's table kernel
+    (programmatic dependent launch); measured on B200, an event pair between
+    turns costs a one-head turn 4-8 us.  A GPU sleep of ``LEAD_CYCLES`` queued
+    before the start event keeps the stream busy while the host packs the
+    first turn, so the region holds no idle time from that packing.
     Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms,
     launches); with ``detail``, also every rank's device ms per turn, mean
     sampled kernel ms and host (issuing) ms per turn."""
-    stride = max(8, -(-steps // 3))
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(0, steps, stride)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def pair():
+        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    sampled = {0: pair()}
+    if steps > 1:
+        sampled[steps - 1] = pair()
+    start, end = pair()
     ranks.barrier()
     torch.cuda.synchronize()
     launches = 0
+    torch.cuda._sleep(LEAD_CYCLES)
     t0 = time.perf_counter()
     start.record()
     for i in range(steps):
-        n, _ = step(kev[i // stride] if i % stride == 0 else None)
+        n, _ = step(sampled.get(i))
         launches += n
     end.record()
     host_ms = (time.perf_counter() - t0) * 1e3
     torch.cuda.synchronize()
     ranks.barrier()
     mine = start.elapsed_time(end)
-    kernel = [x.elapsed_time(y) for x, y in kev]
+    kernel = [x.elapsed_time(y) for x, y in sampled.values()]
     if detail is not None:
         rows = ranks.gather([mine / steps, statistics.mean(kernel), host_ms / steps])
         detail.update({"ms_per_step": [round(r[0], 4) for r in rows],
                        "kernel_ms": [round(r[1], 4) for r in rows],
                        "host_issue_ms_per_step": [round(r[2], 4) for r in rows]})
     return ranks.max(mine), kernel, launches
+
+
+def isolated_turns(step, n: int, ranks: Ranks) -> dict:
+    """``n`` turns each bracketed by its own CUDA events, after the timed region:
+    the best and median single-turn time (max over ranks per turn).  Each turn
+    starts cold (the event before it ends the programmatic overlap with the
+    previous turn), so these are a little above the back-to-back mean."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n)]
+    ranks.barrier()
+    torch.cuda.synchronize()
+    for pair in ev:
+        step(pair)
+    torch.cuda.synchronize()
+    ms = [ranks.max(a.elapsed_time(b)) for a, b in ev]
+    return {"n": n, "best_ms": round(min(ms), 4), "median_ms": round(statistics.median(ms), 4),
+            "spans": "rope_tables_kernel + the load kernel, one turn at a time"}
 
 
 def e2e_turns(worker, jobs, steps: int, ranks: Ranks) -> dict:
@@ -806,6 +837,7 @@ def native_arm(args) -> None:
     rank_bytes = wl.algorithmic_bytes()
     ms_per_step = max_ms / args.steps
     value = turn_bytes / (ms_per_step / 1e3) / 1e9
+    isolated = isolated_turns(step, 10, ranks)
 
     # the alternative load kernel (TMA bulk copies), kernel alone, same turn
     alt = None
@@ -871,6 +903,7 @@ def native_arm(args) -> None:
                     "bulk_load_kernel (mshift_load, TMA)" if fp8
                     else "move_kernel<load> (mshift_load)")
     roof["alternatives"] = alt
+    roof["isolated_turns"] = isolated
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         base = CpuPath(cfg)

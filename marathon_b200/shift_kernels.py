@@ -318,8 +318,9 @@ class _Staging:
 
     A batch's descriptors — run records, store pointer table, capacities,
     deltas, host block tables and a zeroed error word — reach the device in
-    ONE host-to-device copy.  Slots rotate (two by default) so the next batch
-    can be packed while earlier batches' kernels still read theirs.  The copies
+    ONE host-to-device copy.  Slots rotate (four by default for a launcher) so
+    the host can pack batches while earlier batches' kernels still read theirs,
+    up to that many batches ahead of the GPU.  The copies
     go through ``mshift_stage`` (one ``cudaMemcpyAsync`` each) with records
     prepared once per slot.
     """
@@ -452,7 +453,7 @@ class Launcher:
     """
 
     def __init__(self, layers: KVLayers, tile_tokens: int | None = None,
-                 staging_slots: int = 2) -> None:
+                 staging_slots: int = 4) -> None:
         if layers.k_ptrs is None:
             raise ShiftError("the batched kernels need CUDA caches")
         self.layers = layers
