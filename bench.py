@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tile-tokens", type=int, default=0)
     ap.add_argument("--layers", type=int, default=0, help="fewer layers (profiling cases)")
+    ap.add_argument("--rank-share", type=int, default=0, metavar="N",
+                    help="one GPU runs rank 0's head shard of an N-way split (profiling the "
+                         "per-rank launch of an N-GPU run); the line reports that share")
     ap.add_argument("--no-save", action="store_true", help="skip the save-kernel timing")
     ap.add_argument("--no-alt", action="store_true", help="skip the TMA bulk-load timing")
     ap.add_argument("--no-host-tier", action="store_true",
@@ -81,11 +84,26 @@ def parse():
     return ap.parse_args()
 
 
-def workload_config(cfg, world: int, layout: str) -> dict:
-    """The ``config`` object of both arms' lines: the workload only, identical in both."""
+def workload_config(cfg, world: int, layout: str, share: int = 0) -> dict:
+    """The ``config`` object of both arms' lines: the workload only, identical in both.
+
+    ``share`` > 1: one GPU runs rank 0's head shard of a ``share``-way split
+    (a profiling case); the turn bytes are that shard's."""
     from marathon_b200.sharding import head_shard
 
-    lo, hi = head_shard(cfg.heads, 0, world)
+    lo, hi = head_shard(cfg.heads, 0, share or world)
+    if share:
+        return {
+            "workload": f"{cfg.name} {cfg.model} shift turn, rank 0's share of {share}",
+            "layers": cfg.layers, "sessions": cfg.sessions,
+            "tokens_shifted": cfg.shifted_tokens,
+            "deltas": sorted({s.delta for segs in cfg.segments for s in segs}),
+            "heads": cfg.heads, "heads_per_rank": hi - lo, "head_size": cfg.head_size,
+            "block_size": cfg.block_size, "kv_dtype": cfg.dtype, "layout": layout,
+            "parallelism": f"kv-head shard 1 of {share}, on one GPU",
+            "turn_bytes": cfg.algorithmic_bytes(hi - lo),
+            "l2": "inputs larger than L2 (store + paged cache per step >> 126 MB)",
+        }
     return {
         "workload": f"{cfg.name} {cfg.model} shift turn", "layers": cfg.layers,
         "sessions": cfg.sessions, "tokens_shifted": cfg.shifted_tokens,
@@ -805,7 +823,8 @@ def native_arm(args) -> None:
     cfg = config(args.config)
     if args.layers:
         cfg = scaled(cfg, args.layers)
-    h_lo, h_hi = head_shard(cfg.heads, rank, world)
+    share = args.rank_share if world == 1 and args.rank_share > 1 else 0
+    h_lo, h_hi = head_shard(cfg.heads, 0, share) if share else head_shard(cfg.heads, rank, world)
     # store rows of every session plus a paged cache of about the same size,
     # per rank (bytes_per_token_layer counts a row twice: read and write)
     need = sum(cfg.history) * cfg.layers * cfg.bytes_per_token_layer(h_hi - h_lo)
@@ -845,8 +864,9 @@ def native_arm(args) -> None:
     per_rank: dict = {}
     max_ms, per_step, launches = timed_turns(step, args.steps, ranks, per_rank)
     clk = clocks.stop()
-    turn_bytes = cfg.algorithmic_bytes()  # the whole turn, all heads, all ranks
     rank_bytes = wl.algorithmic_bytes()
+    # the whole turn, all heads, all ranks (with --rank-share: that share only)
+    turn_bytes = rank_bytes if share else cfg.algorithmic_bytes()
     ms_per_step = max_ms / args.steps
     value = turn_bytes / (ms_per_step / 1e3) / 1e9
     isolated = isolated_turns(step, 10, ranks)
@@ -903,7 +923,7 @@ def native_arm(args) -> None:
                "status_read": "each step's 4-byte status is copied back every step and read "
                               "on the host once the next step is queued; the last inside "
                               "the timed region"}
-        if world == 1 and not args.no_host_tier:
+        if world == 1 and not share and not args.no_host_tier:
             host_tier = host_tier_timing(cfg, wl, args, names, jobs, fp8, turn_bytes, device)
         del worker, jobs
 
@@ -917,7 +937,7 @@ def native_arm(args) -> None:
     roof["alternatives"] = alt
     roof["isolated_turns"] = isolated
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not share and not args.no_cpu_baseline:
         base = CpuPath(cfg)
         smp = base.sample(args.cpu_seconds)
         cpu = {"value": round(smp["gbs"], 3), "unit": "GB/s", "cores": base.threads,
@@ -929,7 +949,7 @@ def native_arm(args) -> None:
     torch.cuda.empty_cache()
 
     extra = {}
-    if not args.no_extra and args.config == "c2" and not args.layers:
+    if not args.no_extra and args.config == "c2" and not args.layers and not share:
         if world == 1:
             extra["c3"] = c3_extra(args, ranks)
         else:
@@ -949,7 +969,7 @@ def native_arm(args) -> None:
             "vs_baseline": None,
             "dtype": "e4m3" if fp8 else "bf16",
             "data": "synthetic",
-            "config": workload_config(cfg, world, args.layout),
+            "config": workload_config(cfg, world, args.layout, share),
             "gib_s": round(turn_bytes / (ms_per_step / 1e3) / 2**30, 2),
             "launch": {"tile_tokens": tile_tokens},
             "roofline": roof,
