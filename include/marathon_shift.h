@@ -141,6 +141,7 @@ MSHIFT_API int mshift_scatter_shifted(const void* src, int64_t src_tok_stride,
  * read and may be NULL.
  * tiles_per_layer = sum over runs of ceil(len / tile_tokens); each run's
  * tile_begin is the exclusive prefix of that sum (mshift_plan_tiles fills it).
+ * tile_tokens is 1..512 (else MSHIFT_EINVAL); mshift_save takes the same.
  * With n_tables > 0 the kernel is launched with programmatic stream
  * serialization: its CTAs may start while the kernel just before it in the
  * stream (normally mshift_rope_tables) finishes, and wait for that kernel's

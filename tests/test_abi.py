@@ -94,6 +94,10 @@ def test_argument_errors_return_before_any_launch(lib):
     assert lib.mshift_load(p, 128, 16, 1, 0, 1, 1, 8, 8, 1, 2048, 256, 8, 8, None, 0, None,
                            8, None) == _lib.EINVAL
     assert lib.mshift_save(p, 16, 1, 32, 1, 0, 8, 8, 1, 2048, 256, 8, 8, 8, None) == _lib.EINVAL
+    # tiles of more than 512 tokens
+    assert lib.mshift_load(p, 128, 16, 1, 513, 1, 1, 8, 8, 1, 2048, 256, 8, 8, None, 0, None,
+                           8, None) == _lib.EINVAL
+    assert lib.mshift_save(p, 16, 1, 513, 1, 1, 8, 8, 1, 2048, 256, 8, 8, 8, None) == _lib.EINVAL
     # strides that are not whole 16-byte vectors
     bad = _lib.Paged(4096, 2048, 255, 10, 16, 8, 128, _lib.BF16)
     assert lib.mshift_save(bad, 16, 1, 32, 1, 1, 8, 8, 1, 2048, 256, 8, 8, 8, None) == _lib.EINVAL
