@@ -21,9 +21,8 @@ Printed JSON keys beyond the driver's base contract:
   roofline      load kernel: algorithmic bytes per launch / its average launch
                 duration over the timed region (region device time / the
                 launches in it, back to back), against the measured HBM copy
-                peak; sampled_turns_ms: the region's first and last turns
-                between their own events; isolated_turns: best and median of
-                10 single event-timed turns after the timed region
+                peak; isolated_turns: best and median of 10 single
+                event-timed turns after the timed region
   e2e           the same turn through the public worker API (ShiftWorker.load)
                 from host metadata: block table + descriptors copied from pinned
                 host memory, tables + load kernels, the 4-byte status read back;
@@ -564,44 +563,35 @@ def timed_turns(step, steps: int, ranks: Ranks, detail: dict | None = None):
     """``steps`` turns back to back, CUDA events around all of them (barrier and
     sync on both sides), max over ranks.
 
-    Kernel durations are sampled on the first and the last turn.  Their outer
-    events coincide with the region's own, so only two turn boundaries lose
-    the overlap of a load kernel with the next turn's table kernel
-    (programmatic dependent launch); measured on B200, an event pair between
-    turns costs a one-head turn 4-8 us.  A GPU sleep of ``LEAD_CYCLES`` queued
-    before the start event keeps the stream busy while the host packs the
-    first turn, so the region holds no idle time from that packing.
-    Returns (max-over-ranks ms for all turns, this rank's sampled kernel ms,
-    launches); with ``detail``, also every rank's device ms per turn, mean
-    sampled kernel ms and host (issuing) ms per turn."""
-    def pair():
-        return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    sampled = {0: pair()}
-    if steps > 1:
-        sampled[steps - 1] = pair()
-    start, end = pair()
+    No event sits between turns: one there ends the overlap of a load kernel
+    with the next turn's table kernel (programmatic dependent launch), which
+    measured on B200 costs a one-head turn 4-8 us; single-turn times come
+    from ``isolated_turns`` after the region instead.  A GPU sleep of
+    ``LEAD_CYCLES`` queued before the start event keeps the stream busy while
+    the host packs the first turn, so the region holds no idle time from that
+    packing.  Returns (max-over-ranks ms for all turns, launches); with
+    ``detail``, also every rank's device ms and host (issuing) ms per turn."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
     ranks.barrier()
     torch.cuda.synchronize()
     launches = 0
     torch.cuda._sleep(LEAD_CYCLES)
     t0 = time.perf_counter()
     start.record()
-    for i in range(steps):
-        n, _ = step(sampled.get(i))
+    for _ in range(steps):
+        n, _ = step(None)
         launches += n
     end.record()
     host_ms = (time.perf_counter() - t0) * 1e3
     torch.cuda.synchronize()
     ranks.barrier()
     mine = start.elapsed_time(end)
-    kernel = [x.elapsed_time(y) for x, y in sampled.values()]
     if detail is not None:
-        rows = ranks.gather([mine / steps, statistics.mean(kernel), host_ms / steps])
+        rows = ranks.gather([mine / steps, host_ms / steps])
         detail.update({"ms_per_step": [round(r[0], 4) for r in rows],
-                       "kernel_ms": [round(r[1], 4) for r in rows],
-                       "host_issue_ms_per_step": [round(r[2], 4) for r in rows]})
-    return ranks.max(mine), kernel, launches
+                       "host_issue_ms_per_step": [round(r[1], 4) for r in rows]})
+    return ranks.max(mine), launches
 
 
 def isolated_turns(step, n: int, ranks: Ranks) -> dict:
@@ -663,18 +653,15 @@ def worker_for(wl, cfg, layout, device, fp8):
     return worker, jobs, names
 
 
-def roofline(rank_bytes: int, launch_ms: float, sampled_ms: list[float], traffic,
-             kernel: str) -> dict:
+def roofline(rank_bytes: int, launch_ms: float, traffic, kernel: str) -> dict:
     """The load kernel against the HBM roofline.
 
     ``launch_ms`` is the kernel's average launch duration over the timed
     region: the region's device time (CUDA events, max over ranks) over the
     load launches in it, one per turn, back to back; the turn's table kernel
-    (about 3 us) overlaps the previous load through programmatic dependent
+    (about 3-5 us) overlaps the previous load through programmatic dependent
     launch, and the ncu launch list gives the load kernel 99.7% of a turn's
-    kernel time.  ``sampled_ms`` are the first and last turns of the region,
-    each between its own events (each of those loses the overlap with a
-    neighbouring turn, so they read a little slower).
+    kernel time.
     """
     peak, peak_kind = peaks()
     achieved = rank_bytes / (launch_ms / 1e3) / 1e9
@@ -685,9 +672,6 @@ def roofline(rank_bytes: int, launch_ms: float, sampled_ms: list[float], traffic
         "kernel_ms": round(launch_ms, 4),
         "kernel_ms_spans": "timed region device time (max over ranks) / load launches in it; "
                            "launches back to back, the table kernel overlapping",
-        "sampled_turns_ms": [round(x, 4) for x in sampled_ms],
-        "sampled_turns_spans": "first and last turns: table + load kernel between their own "
-                               "CUDA events",
         "bytes_per_launch": rank_bytes,
         "traffic": round(traffic) if traffic else None,
     }
@@ -746,24 +730,24 @@ def c3_extra(args, ranks: Ranks) -> dict:
     for _ in range(args.warmup):
         load_step(launcher, wl)
     steps = max(args.steps, 10)
-    total_ms, kernel_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
+    total_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
     ms = total_ms / steps
     out = {"config": workload_config(cfg, 1, args.layout), "metric": METRIC,
            "value": round(cfg.algorithmic_bytes() / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
            "ms_per_step": round(ms, 4), "steps": steps, "target_ms": 0.781,
-           "roofline": roofline(wl.algorithmic_bytes(), ms, kernel_ms,
+           "roofline": roofline(wl.algorithmic_bytes(), ms,
                                 traffic_for(cfg.name, args.layout,
                                             cfg.shifted_tokens * cfg.layers),
                                 "bulk_load_kernel (mshift_load, TMA)")}
     prev = set_load_kernel("lsu")
     try:
-        _, lsu_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), 10, ranks)
+        lsu_total, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), 10, ranks)
     finally:
         set_load_kernel(prev)
+    lsu_ms = lsu_total / 10
     out["roofline"]["alternatives"] = {"lsu": {
-        "kernel": "move_kernel<load> (128-bit loads)",
-        "kernel_ms": round(statistics.mean(lsu_ms), 4),
-        "achieved": round(wl.algorithmic_bytes() / (statistics.mean(lsu_ms) / 1e3) / 1e9, 1)}}
+        "kernel": "move_kernel<load> (128-bit loads)", "kernel_ms": round(lsu_ms, 4),
+        "achieved": round(wl.algorithmic_bytes() / (lsu_ms / 1e3) / 1e9, 1)}}
     worker, jobs, _ = worker_for(wl, cfg, args.layout, ranks.device, True)
     e = e2e_turns(worker, jobs, max(10, min(args.steps, 100)), ranks)
     out["e2e"] = {"value": round(cfg.algorithmic_bytes() / (e["ms_per_step"] / 1e3) / 1e9, 2),
@@ -802,12 +786,12 @@ def c4_extra(args, ranks: Ranks) -> dict:
     for _ in range(args.warmup):
         load_step(launcher, wl)
     steps = max(args.steps, 10)
-    total_ms, kernel_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
+    total_ms, _ = timed_turns(lambda ev: load_step(launcher, wl, ev), steps, ranks)
     ms = total_ms / steps
     out = {"config": workload_config(cfg, ranks.world, args.layout), "metric": METRIC,
            "value": round(cfg.algorithmic_bytes() / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
            "ms_per_step": round(ms, 4), "steps": steps, "runs": len(wl.runs),
-           "roofline": roofline(wl.algorithmic_bytes(), ms, kernel_ms, None,
+           "roofline": roofline(wl.algorithmic_bytes(), ms, None,
                                 "move_kernel<load> (mshift_load)")}
     worker, jobs, _ = worker_for(wl, cfg, args.layout, ranks.device, False)
     e = e2e_turns(worker, jobs, max(10, min(args.steps, 50)), ranks)
@@ -871,7 +855,7 @@ def native_arm(args) -> None:
             step()
         torch.cuda.synchronize()
     per_rank: dict = {}
-    max_ms, per_step, launches = timed_turns(step, args.steps, ranks, per_rank)
+    max_ms, launches = timed_turns(step, args.steps, ranks, per_rank)
     clk = clocks.stop()
     rank_bytes = wl.algorithmic_bytes()
     # the whole turn, all heads, all ranks (with --rank-share: that share only)
@@ -888,10 +872,11 @@ def native_arm(args) -> None:
         prev = set_load_kernel("lsu" if fp8 else "bulk")  # the one auto did not pick
         try:
             load_step(launcher, wl, check=True)
-            _, a_ms, _ = timed_turns(step, max(10, min(args.steps, 100)), ranks)
+            n_alt = max(10, min(args.steps, 100))
+            a_total, _ = timed_turns(step, n_alt, ranks)
             name = ("lsu", "move_kernel<load> (128-bit loads)") if fp8 else (
                 "bulk", "bulk_load_kernel (TMA cp.async.bulk, mbarrier ring)")
-            m = statistics.mean(a_ms)
+            m = a_total / n_alt
             alt = {name[0]: {"kernel": name[1], "kernel_ms": round(m, 4),
                              "achieved": round(rank_bytes / (m / 1e3) / 1e9, 1)}}
         finally:
@@ -940,7 +925,7 @@ def native_arm(args) -> None:
     traffic = traffic_for(cfg.name, args.layout, units)
     if traffic is not None:
         traffic *= (h_hi - h_lo) / cfg.heads  # this rank's head shard of each unit
-    roof = roofline(rank_bytes, ms_per_step, per_step, traffic,
+    roof = roofline(rank_bytes, ms_per_step, traffic,
                     "bulk_load_kernel (mshift_load, TMA)" if fp8
                     else "move_kernel<load> (mshift_load)")
     roof["alternatives"] = alt
